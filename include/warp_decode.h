@@ -1,0 +1,142 @@
+/*
+ * warp_decode_b200 — C ABI for the fused MoE decode kernels on B200 (sm_100a).
+ *
+ * This header is the drop-in boundary.  Every entry point takes plain device
+ * pointers, sizes and a CUDA stream handle (passed as `void*`, i.e. the value
+ * of a `cudaStream_t`; NULL means the legacy default stream).  Nothing here
+ * allocates device memory, synchronises the stream, or depends on PyTorch.
+ *
+ * Reference interfaces replaced (Religious-J/warp_decode):
+ *   wd_moe_gate_up_3d_batched  <- warp_decode::launch_moe_gate_up_3d_batched
+ *                                 csrc/moe_gate_up_3d_batched.cu:117-131
+ *                                 (host checks it inherits: csrc/binding.cpp:35-73)
+ *   wd_moe_down_3d_batched     <- warp_decode::launch_moe_down_3d_batched
+ *                                 csrc/moe_down_3d_batched.cu:124-141
+ *                                 (host checks it inherits: csrc/binding.cpp:79-121)
+ *   wd_moe_*_mxfp8             <- no counterpart in the reference; the MXFP8
+ *                                 weight format is listed as future work in
+ *                                 README.md:294-308 of the reference.
+ *
+ * Layouts (all row-major, contiguous):
+ *   x          [B, hidden]               bf16
+ *   w_gate_up  [E, 2*inter, hidden]      bf16  rows [0,inter) gate, [inter,2*inter) up
+ *   topk_ids   [B, topk]                 int32
+ *   h (buffer) [B*topk, inter]           bf16  h = silu(x.gate) * (x.up)
+ *   w_down     [E, hidden, inter]        bf16
+ *   topk_scale [B, topk]                 fp32
+ *   y (out)    [B, hidden]               bf16 (or fp32 for tensor-parallel partials)
+ *
+ * MXFP8 weights (OCP Microscaling v1.0, MXFP8 E4M3, block size 32 along the
+ * reduction axis):
+ *   gate_up:  q [E, 2*inter, hidden] uint8 (e4m3), s [E, 2*inter, hidden/32] uint8 (ue8m0)
+ *   down:     q [E, hidden, inter]   uint8 (e4m3), s [E, hidden, inter/32]   uint8 (ue8m0)
+ *   value = e4m3(q) * 2^(s - 127)
+ *
+ * Error behaviour: every entry point validates its arguments on the host and
+ * returns WD_OK or a wd_error_t code without launching anything on failure;
+ * wd_last_error_message() then holds a human-readable reason (thread-local).
+ * Device-side conditions that the host cannot see (an expert id outside
+ * [0, E), a bounded wait that gave up) are OR-ed into a 32-bit status word:
+ * either the caller's `status` (device pointer) or, when that is NULL, a
+ * per-device word owned by the library (read it with wd_status_read).
+ * Slots whose expert id is out of range contribute zeros and are never used
+ * to address weight memory.
+ */
+#ifndef WARP_DECODE_B200_H_
+#define WARP_DECODE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__) || defined(__clang__)
+#define WD_API __attribute__((visibility("default")))
+#else
+#define WD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum wd_error_t {
+  WD_OK = 0,
+  WD_ERR_NULL_POINTER = 1,   /* a required pointer is NULL                     */
+  WD_ERR_SHAPE = 2,          /* sizes are negative, zero or inconsistent        */
+  WD_ERR_ALIGNMENT = 3,      /* a pointer is not 16-byte aligned                */
+  WD_ERR_UNSUPPORTED = 4,    /* shape outside what the kernels implement        */
+  WD_ERR_CUDA = 5            /* a CUDA runtime call or kernel launch failed     */
+} wd_error_t;
+
+/* Bits of the device status word. */
+#define WD_STATUS_BAD_EXPERT_ID   0x1u  /* some topk_ids entry was outside [0, E)   */
+#define WD_STATUS_WAIT_TIMEOUT    0x2u  /* a bounded pipeline wait gave up          */
+#define WD_STATUS_ROUTING_CHANGED 0x4u  /* down saw topk_ids change under an early
+                                           start and recomputed (informational)   */
+
+/* Library version, as MAJOR*10000 + MINOR*100 + PATCH. */
+WD_API int wd_version(void);
+
+/* Static description of an error code. */
+WD_API const char* wd_error_string(int err);
+
+/* Detail message of the last failing call on this host thread ("" if none). */
+WD_API const char* wd_last_error_message(void);
+
+/*
+ * gate_up + silu_and_mul, fused:
+ *   h[b*topk+s, n] = silu(sum_k x[b,k] W[e,n,k]) * sum_k x[b,k] W[e,inter+n,k],  e = topk_ids[b,s]
+ * FP32 accumulation, bf16 output.  Requirements: hidden % 8 == 0, inter >= 1,
+ * 1 <= topk <= 512, x / w_gate_up 16-byte aligned.
+ * Replaces warp_decode::launch_moe_gate_up_3d_batched (csrc/moe_gate_up_3d_batched.cu:117-131).
+ */
+WD_API int wd_moe_gate_up_3d_batched(const void* x, const void* w_gate_up,
+                              const int32_t* topk_ids, void* h_out,
+                              int B, int E, int topk, int hidden, int inter,
+                              uint32_t* status, void* stream);
+
+/*
+ * down projection + top-k weighted sum, fused:
+ *   y[b, j] = sum_s topk_scale[b,s] * sum_i h[b*topk+s, i] W[e,j,i],  e = topk_ids[b,s]
+ * FP32 products and accumulation.  out_fp32 = 0 writes bf16, 1 writes fp32
+ * (un-rounded tensor-parallel partial sums).  Requirements: inter % 8 == 0,
+ * 1 <= topk <= 512, h / w_down 16-byte aligned.
+ * The launch may start early behind a directly preceding
+ * wd_moe_gate_up_3d_batched on the same stream (programmatic dependent
+ * launch) and prefetch w_down rows; it reads h and topk_scale only after the
+ * preceding kernel has finished, and re-checks topk_ids then.
+ * Replaces warp_decode::launch_moe_down_3d_batched (csrc/moe_down_3d_batched.cu:124-141).
+ */
+WD_API int wd_moe_down_3d_batched(const void* h, const void* w_down,
+                           const int32_t* topk_ids, const float* topk_scale,
+                           void* y_out, int out_fp32,
+                           int B, int E, int topk, int hidden, int inter,
+                           uint32_t* status, void* stream);
+
+/*
+ * MXFP8-weight variants (no counterpart in the reference).  Activations stay
+ * bf16; weights are dequantised in registers (e4m3 * 2^(s-127)) and the dot
+ * products accumulate in FP32.  Extra requirements: hidden % 32 == 0
+ * (gate_up) / inter % 32 == 0 (down), and the scale tensor's byte size a
+ * multiple of 16.
+ */
+WD_API int wd_moe_gate_up_3d_batched_mxfp8(const void* x, const uint8_t* w_q, const uint8_t* w_scale,
+                                    const int32_t* topk_ids, void* h_out,
+                                    int B, int E, int topk, int hidden, int inter,
+                                    uint32_t* status, void* stream);
+
+WD_API int wd_moe_down_3d_batched_mxfp8(const void* h, const uint8_t* w_q, const uint8_t* w_scale,
+                                 const int32_t* topk_ids, const float* topk_scale,
+                                 void* y_out, int out_fp32,
+                                 int B, int E, int topk, int hidden, int inter,
+                                 uint32_t* status, void* stream);
+
+/*
+ * Read (and optionally clear) the library-owned status word of the current
+ * CUDA device.  Synchronous: it waits for work already queued on the device.
+ */
+WD_API int wd_status_read(uint32_t* value, int clear);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* WARP_DECODE_B200_H_ */

@@ -1,0 +1,134 @@
+"""ctypes binding of the C ABI in ``include/warp_decode.h``.
+
+This is the binding a non-PyTorch host would write; the
+tests use it to drive the kernels through the exact C entry points.  Pointers
+are plain integers (device addresses), streams are ``cudaStream_t`` values.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+from . import _build
+
+WD_OK = 0
+WD_ERR_NULL_POINTER = 1
+WD_ERR_SHAPE = 2
+WD_ERR_ALIGNMENT = 3
+WD_ERR_UNSUPPORTED = 4
+WD_ERR_CUDA = 5
+
+WD_STATUS_BAD_EXPERT_ID = 0x1
+WD_STATUS_WAIT_TIMEOUT = 0x2
+WD_STATUS_ROUTING_CHANGED = 0x4
+
+HEADER = _build.INCLUDE / "warp_decode.h"
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIGS = {
+    "wd_version": (_I, []),
+    "wd_error_string": (ctypes.c_char_p, [_I]),
+    "wd_last_error_message": (ctypes.c_char_p, []),
+    "wd_moe_gate_up_3d_batched": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "wd_moe_down_3d_batched": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "wd_moe_gate_up_3d_batched_mxfp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "wd_moe_down_3d_batched_mxfp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "wd_status_read": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+}
+
+_lib = None
+
+
+def header_symbols(path: Path = HEADER) -> list[str]:
+    """Names of every function the header declares with WD_API."""
+    text = path.read_text()
+    return re.findall(r"^WD_API\s+[^;(]*?\b(wd_\w+)\s*\(", text, flags=re.M)
+
+
+def lib() -> ctypes.CDLL:
+    """Load libwarp_decode_b200.so (the same instance the torch extension uses)."""
+    global _lib
+    if _lib is None:
+        if not _build.LIB.exists():
+            raise OSError(f"{_build.LIB} is not built; run `python -m warp_decode_b200._build`")
+        L = ctypes.CDLL(str(_build.LIB))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+class WarpDecodeError(RuntimeError):
+    def __init__(self, code: int):
+        L = lib()
+        self.code = code
+        super().__init__(f"{L.wd_error_string(code).decode()}: {L.wd_last_error_message().decode()}")
+
+
+def check(code: int) -> None:
+    if code != WD_OK:
+        raise WarpDecodeError(code)
+
+
+def gate_up(x, w, ids, out, B, E, topk, hidden, inter, status=None, stream=0) -> int:
+    return lib().wd_moe_gate_up_3d_batched(x, w, ids, out, B, E, topk, hidden, inter, status, stream)
+
+
+def down(h, w, ids, scale, out, out_fp32, B, E, topk, hidden, inter, status=None, stream=0) -> int:
+    return lib().wd_moe_down_3d_batched(h, w, ids, scale, out, out_fp32, B, E, topk, hidden, inter,
+                                        status, stream)
+
+
+def gate_up_mxfp8(x, wq, ws, ids, out, B, E, topk, hidden, inter, status=None, stream=0) -> int:
+    return lib().wd_moe_gate_up_3d_batched_mxfp8(x, wq, ws, ids, out, B, E, topk, hidden, inter,
+                                                 status, stream)
+
+
+def down_mxfp8(h, wq, ws, ids, scale, out, out_fp32, B, E, topk, hidden, inter, status=None,
+               stream=0) -> int:
+    return lib().wd_moe_down_3d_batched_mxfp8(h, wq, ws, ids, scale, out, out_fp32, B, E, topk,
+                                              hidden, inter, status, stream)
+
+
+def status_read(clear: bool = True) -> int:
+    v = ctypes.c_uint32(0)
+    check(lib().wd_status_read(ctypes.byref(v), 1 if clear else 0))
+    return int(v.value)
+
+
+# ---------------------------------------------------------------------------
+# torch-tensor conveniences (device pointers + current stream)
+# ---------------------------------------------------------------------------
+def _stream():
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream
+
+
+def torch_gate_up(x, w, ids):
+    """moe_gate_up_3d_batched through the C ABI (torch tensors in, tensor out)."""
+    import torch
+
+    B, H = x.shape
+    E, two_i, _ = w.shape
+    K = ids.shape[1]
+    out = torch.empty(B * K, two_i // 2, dtype=torch.bfloat16, device=x.device)
+    check(gate_up(x.data_ptr(), w.data_ptr(), ids.data_ptr(), out.data_ptr(), B, E, K, H,
+                  two_i // 2, None, _stream()))
+    return out
+
+
+def torch_down(h, w, ids, scale, fp32_out=False):
+    """moe_down_3d_batched through the C ABI."""
+    import torch
+
+    B, K = ids.shape
+    E, H, I = w.shape
+    out = torch.empty(B, H, dtype=torch.float32 if fp32_out else torch.bfloat16, device=h.device)
+    check(down(h.data_ptr(), w.data_ptr(), ids.data_ptr(), scale.data_ptr(), out.data_ptr(),
+               1 if fp32_out else 0, B, E, K, H, I, None, _stream()))
+    return out

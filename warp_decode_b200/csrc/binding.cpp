@@ -1,0 +1,204 @@
+// PyTorch extension surface of warp_decode_b200.
+//
+// Same function names, argument order and tensor contracts as the reference
+// binding (csrc/binding.cpp:35-130 of Religious-J/warp_decode):
+//   moe_gate_up_3d_batched(x[B,H] bf16, w[E,2I,H] bf16, topk_ids[B,K] int32) -> [B*K, I] bf16
+//   moe_down_3d_batched(buffer[B*K,I] bf16, w[E,H,I] bf16, topk_ids[B,K] int32,
+//                       topk_scale[B,K] fp32, B) -> [B, H] bf16
+// Validation failures raise RuntimeError (TORCH_CHECK) before any launch,
+// with the reference's messages for the checks the two share.  The output is
+// allocated with the caching allocator and the kernels run on the current
+// stream; nothing synchronises.  All compute goes through the C ABI in
+// libwarp_decode_b200.so (include/warp_decode.h).
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "warp_decode.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be CUDA")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be fp32")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+#define CHECK_U8(x) TORCH_CHECK((x).scalar_type() == at::kByte, #x " must be uint8")
+
+void check_same_device(const torch::Tensor& a, const torch::Tensor& b, const char* name) {
+  TORCH_CHECK(a.device() == b.device(), name, " must be on the same device as the first input");
+}
+
+void check_rc(int rc) {
+  TORCH_CHECK(rc == WD_OK, "warp_decode: ", wd_error_string(rc), ": ", wd_last_error_message());
+}
+
+int to_int(int64_t v, const char* what) {
+  TORCH_CHECK(v >= 0 && v <= INT32_MAX, what, " out of int32 range");
+  return static_cast<int>(v);
+}
+
+void* stream_ptr() { return reinterpret_cast<void*>(at::cuda::getCurrentCUDAStream().stream()); }
+
+// Shared checks and shapes of the two gate_up entry points.
+struct GateUpShape {
+  int B, E, topk, hidden, inter;
+};
+
+GateUpShape gate_up_shape(const torch::Tensor& x, const torch::Tensor& w,
+                          const torch::Tensor& topk_ids, bool mx) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_BF16(x);
+  CHECK_CUDA(w); CHECK_CONTIG(w);
+  if (mx) { CHECK_U8(w); } else { CHECK_BF16(w); }
+  CHECK_CUDA(topk_ids); CHECK_CONTIG(topk_ids); CHECK_I32(topk_ids);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 3 && topk_ids.dim() == 2);
+  check_same_device(x, w, "w");
+  check_same_device(x, topk_ids, "topk_ids");
+  GateUpShape s;
+  s.B = to_int(x.size(0), "B");
+  s.hidden = to_int(x.size(1), "hidden");
+  s.E = to_int(w.size(0), "E");
+  const int two_i = to_int(w.size(1), "2*inter");
+  TORCH_CHECK(two_i % 2 == 0, "w.size(1) must be 2 * inter");
+  s.inter = two_i / 2;
+  TORCH_CHECK(w.size(2) == s.hidden, "w.size(2) must == hidden");
+  TORCH_CHECK(topk_ids.size(0) == s.B);
+  s.topk = to_int(topk_ids.size(1), "topk");
+  return s;
+}
+
+torch::Tensor moe_gate_up_3d_batched(torch::Tensor x, torch::Tensor w, torch::Tensor topk_ids) {
+  const GateUpShape s = gate_up_shape(x, w, topk_ids, false);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto out = torch::empty({(int64_t)s.B * s.topk, s.inter}, x.options().dtype(at::kBFloat16));
+  check_rc(wd_moe_gate_up_3d_batched(x.data_ptr(), w.data_ptr(), topk_ids.data_ptr<int32_t>(),
+                                     out.data_ptr(), s.B, s.E, s.topk, s.hidden, s.inter, nullptr,
+                                     stream_ptr()));
+  return out;
+}
+
+torch::Tensor moe_gate_up_3d_batched_mxfp8(torch::Tensor x, torch::Tensor w_q,
+                                           torch::Tensor w_scale, torch::Tensor topk_ids) {
+  const GateUpShape s = gate_up_shape(x, w_q, topk_ids, true);
+  CHECK_CUDA(w_scale); CHECK_CONTIG(w_scale); CHECK_U8(w_scale);
+  check_same_device(x, w_scale, "w_scale");
+  TORCH_CHECK(s.hidden % 32 == 0, "hidden must be a multiple of 32 for MXFP8 weights");
+  TORCH_CHECK(w_scale.dim() == 3 && w_scale.size(0) == s.E && w_scale.size(1) == 2 * s.inter &&
+                  w_scale.size(2) == s.hidden / 32,
+              "w_scale must be [E, 2*inter, hidden/32]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto out = torch::empty({(int64_t)s.B * s.topk, s.inter}, x.options().dtype(at::kBFloat16));
+  check_rc(wd_moe_gate_up_3d_batched_mxfp8(
+      x.data_ptr(), w_q.data_ptr<uint8_t>(), w_scale.data_ptr<uint8_t>(),
+      topk_ids.data_ptr<int32_t>(), out.data_ptr(), s.B, s.E, s.topk, s.hidden, s.inter, nullptr,
+      stream_ptr()));
+  return out;
+}
+
+struct DownShape {
+  int B, E, topk, hidden, inter;
+};
+
+DownShape down_shape(const torch::Tensor& buffer, const torch::Tensor& w,
+                     const torch::Tensor& topk_ids, const torch::Tensor& topk_scale,
+                     c10::optional<int64_t> B_arg, bool mx) {
+  CHECK_CUDA(buffer); CHECK_CONTIG(buffer); CHECK_BF16(buffer);
+  CHECK_CUDA(w); CHECK_CONTIG(w);
+  if (mx) { CHECK_U8(w); } else { CHECK_BF16(w); }
+  CHECK_CUDA(topk_ids); CHECK_CONTIG(topk_ids); CHECK_I32(topk_ids);
+  CHECK_CUDA(topk_scale); CHECK_CONTIG(topk_scale); CHECK_F32(topk_scale);
+  TORCH_CHECK(buffer.dim() == 2 && w.dim() == 3 && topk_ids.dim() == 2 && topk_scale.dim() == 2);
+  check_same_device(buffer, w, "w");
+  check_same_device(buffer, topk_ids, "topk_ids");
+  check_same_device(buffer, topk_scale, "topk_scale");
+  DownShape s;
+  s.B = B_arg.has_value() ? to_int(*B_arg, "B") : to_int(topk_ids.size(0), "B");
+  s.inter = to_int(buffer.size(1), "inter");
+  s.E = to_int(w.size(0), "E");
+  s.hidden = to_int(w.size(1), "hidden");
+  TORCH_CHECK(w.size(2) == s.inter, "w.size(2) must == inter");
+  TORCH_CHECK(topk_ids.size(0) == s.B);
+  s.topk = to_int(topk_ids.size(1), "topk");
+  TORCH_CHECK(topk_scale.size(0) == s.B && topk_scale.size(1) == s.topk);
+  TORCH_CHECK(buffer.size(0) == (int64_t)s.B * s.topk, "buffer rows must be B*topk");
+  return s;
+}
+
+torch::Tensor down_common(torch::Tensor buffer, torch::Tensor w, c10::optional<torch::Tensor> w_scale,
+                          torch::Tensor topk_ids, torch::Tensor topk_scale,
+                          c10::optional<int64_t> B_arg, bool fp32_out) {
+  const bool mx = w_scale.has_value();
+  const DownShape s = down_shape(buffer, w, topk_ids, topk_scale, B_arg, mx);
+  if (mx) {
+    const auto& sc = *w_scale;
+    CHECK_CUDA(sc); CHECK_CONTIG(sc); CHECK_U8(sc);
+    check_same_device(buffer, sc, "w_scale");
+    TORCH_CHECK(s.inter % 32 == 0, "inter must be a multiple of 32 for MXFP8 weights");
+    TORCH_CHECK(sc.dim() == 3 && sc.size(0) == s.E && sc.size(1) == s.hidden &&
+                    sc.size(2) == s.inter / 32,
+                "w_scale must be [E, hidden, inter/32]");
+  }
+  const c10::cuda::CUDAGuard guard(buffer.device());
+  auto out = torch::empty({s.B, s.hidden},
+                          buffer.options().dtype(fp32_out ? at::kFloat : at::kBFloat16));
+  if (mx) {
+    check_rc(wd_moe_down_3d_batched_mxfp8(
+        buffer.data_ptr(), w.data_ptr<uint8_t>(), w_scale->data_ptr<uint8_t>(),
+        topk_ids.data_ptr<int32_t>(), topk_scale.data_ptr<float>(), out.data_ptr(),
+        fp32_out ? 1 : 0, s.B, s.E, s.topk, s.hidden, s.inter, nullptr, stream_ptr()));
+  } else {
+    check_rc(wd_moe_down_3d_batched(buffer.data_ptr(), w.data_ptr(), topk_ids.data_ptr<int32_t>(),
+                                    topk_scale.data_ptr<float>(), out.data_ptr(), fp32_out ? 1 : 0,
+                                    s.B, s.E, s.topk, s.hidden, s.inter, nullptr, stream_ptr()));
+  }
+  return out;
+}
+
+torch::Tensor moe_down_3d_batched(torch::Tensor buffer, torch::Tensor w, torch::Tensor topk_ids,
+                                  torch::Tensor topk_scale, c10::optional<int64_t> B) {
+  return down_common(buffer, w, c10::nullopt, topk_ids, topk_scale, B, false);
+}
+
+torch::Tensor moe_down_3d_batched_partial(torch::Tensor buffer, torch::Tensor w,
+                                          torch::Tensor topk_ids, torch::Tensor topk_scale,
+                                          c10::optional<int64_t> B) {
+  return down_common(buffer, w, c10::nullopt, topk_ids, topk_scale, B, true);
+}
+
+torch::Tensor moe_down_3d_batched_mxfp8(torch::Tensor buffer, torch::Tensor w_q,
+                                        torch::Tensor w_scale, torch::Tensor topk_ids,
+                                        torch::Tensor topk_scale, c10::optional<int64_t> B,
+                                        bool fp32_out) {
+  return down_common(buffer, w_q, w_scale, topk_ids, topk_scale, B, fp32_out);
+}
+
+int64_t status(bool clear, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  uint32_t v = 0;
+  check_rc(wd_status_read(&v, clear ? 1 : 0));
+  return static_cast<int64_t>(v);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  namespace py = pybind11;
+  m.def("moe_gate_up_3d_batched", &moe_gate_up_3d_batched,
+        "Fused MoE gate_up + silu_and_mul (bf16, FP32 accumulation)", py::arg("x"), py::arg("w"),
+        py::arg("topk_ids"));
+  m.def("moe_down_3d_batched", &moe_down_3d_batched,
+        "Fused MoE down projection + top-k weighted sum (bf16 out)", py::arg("buffer"),
+        py::arg("w"), py::arg("topk_ids"), py::arg("topk_scale"), py::arg("B") = py::none());
+  m.def("moe_down_3d_batched_partial", &moe_down_3d_batched_partial,
+        "As moe_down_3d_batched, FP32 output (tensor-parallel partial sums)", py::arg("buffer"),
+        py::arg("w"), py::arg("topk_ids"), py::arg("topk_scale"), py::arg("B") = py::none());
+  m.def("moe_gate_up_3d_batched_mxfp8", &moe_gate_up_3d_batched_mxfp8,
+        "Fused MoE gate_up + silu_and_mul with MXFP8 (e4m3 + ue8m0/32) weights", py::arg("x"),
+        py::arg("w_q"), py::arg("w_scale"), py::arg("topk_ids"));
+  m.def("moe_down_3d_batched_mxfp8", &moe_down_3d_batched_mxfp8,
+        "Fused MoE down + top-k weighted sum with MXFP8 weights", py::arg("buffer"),
+        py::arg("w_q"), py::arg("w_scale"), py::arg("topk_ids"), py::arg("topk_scale"),
+        py::arg("B") = py::none(), py::arg("fp32_out") = false);
+  m.def("status", &status, "Read (and clear) the device status word of the library",
+        py::arg("clear") = true, py::arg("device") = 0);
+}

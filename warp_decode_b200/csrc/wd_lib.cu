@@ -1,0 +1,293 @@
+// C ABI of warp_decode_b200: argument validation, launch geometry and
+// dispatch for the fused MoE decode kernels.  Single translation unit so the
+// library-owned status word needs no relocatable device code.
+//
+// Host-side behaviour mirrors the reference binding (csrc/binding.cpp:35-121):
+// shapes are checked before anything is launched, the output is written on
+// the caller's stream, nothing synchronises.  Differences: errors are return
+// codes (the torch layer turns them into RuntimeError), expert ids are
+// range-checked on the device, and B = 0 is a valid no-op.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "wd_down.cuh"
+#include "wd_gate_up.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int smem_optin = 0;
+  bool ready = false;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+// Per-device setup: SM count, opt-in shared memory and kernel attributes.
+// Runs once per device, on the first call made with that device current.
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return fail(WD_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return fail(WD_ERR_CUDA, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    err = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (err == cudaSuccess)
+      err = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
+    };
+    for (const void* k : kernels) {
+      if (err != cudaSuccess) break;
+      err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin);
+      // Full shared-memory carve-out so a gate_up CTA and an early-started
+      // down CTA fit on one SM together.
+      if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   (int)cudaSharedmemCarveoutMaxShared);
+    }
+    if (err != cudaSuccess)
+      return fail(WD_ERR_CUDA, std::string("device setup: ") + cudaGetErrorString(err));
+    d.ready = true;
+  }
+  *out = &d;
+  return WD_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("WARP_DECODE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int B, int E, int topk, int hidden, int inter) {
+  if (B < 0) return fail(WD_ERR_SHAPE, "B must be >= 0");
+  if (E < 1) return fail(WD_ERR_SHAPE, "E (number of experts) must be >= 1");
+  if (topk < 1) return fail(WD_ERR_SHAPE, "topk must be >= 1");
+  if (topk > wdb::MAX_SLOTS) return fail(WD_ERR_UNSUPPORTED, "topk must be <= 512");
+  if (hidden < 1 || inter < 1) return fail(WD_ERR_SHAPE, "hidden and inter must be >= 1");
+  return WD_OK;
+}
+
+template <int FMT>
+int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const int32_t* ids,
+                 void* out, int B, int E, int topk, int hidden, int inter, uint32_t* status,
+                 void* stream) {
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (FMT == wdb::W_BF16 && hidden % 8 != 0)
+    return fail(WD_ERR_SHAPE, "hidden must be a multiple of 8 (16-byte weight rows)");
+  if (FMT == wdb::W_E4M3 && hidden % 32 != 0)
+    return fail(WD_ERR_SHAPE, "hidden must be a multiple of 32 (MXFP8 block size)");
+  if (B == 0) return WD_OK;
+  if (!x || !w || !ids || !out || (FMT == wdb::W_E4M3 && !wscale))
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(w) || (FMT == wdb::W_E4M3 && !aligned16(wscale)))
+    return fail(WD_ERR_ALIGNMENT, "x and w_gate_up must be 16-byte aligned");
+  if (FMT == wdb::W_E4M3 && ((size_t)E * 2 * inter * (hidden / 32)) % 16 != 0)
+    return fail(WD_ERR_ALIGNMENT, "MXFP8 scale tensor size must be a multiple of 16 bytes");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+
+  using Cfg = wdb::GateUpCfg<FMT>;
+  const int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
+  int nstages = std::min(6, std::max(2, (96 * 1024) / Cfg::STAGE_BYTES));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tb) {
+    const int bn = std::min(tb, B - b0);
+    const int n = bn * topk;
+    const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
+    const int smem = wdb::gate_up_smem_bytes(FMT, nstages, n, E, dedup);
+    if (smem > dev->smem_optin) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    wdb::GateUpArgs a;
+    a.x = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
+    a.w = w;
+    a.wscale = wscale;
+    a.ids = ids + (size_t)b0 * topk;
+    a.out = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)b0 * topk * inter;
+    a.status = status;
+    a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+    a.dedup = dedup ? 1 : 0;
+    a.nstages = nstages;
+    const long long work = (long long)n * inter;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+    cfg.blockDim = dim3(wdb::GU_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_kernel<FMT>, a);
+    if (err != cudaSuccess)
+      return fail(WD_ERR_CUDA, std::string("gate_up launch: ") + cudaGetErrorString(err));
+  }
+  return WD_OK;
+}
+
+template <int FMT>
+int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int32_t* ids,
+              const float* scale, void* out, int out_fp32, int B, int E, int topk, int hidden,
+              int inter, uint32_t* status, void* stream) {
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (FMT == wdb::W_BF16 && inter % 8 != 0)
+    return fail(WD_ERR_SHAPE, "inter must be a multiple of 8 (16-byte weight rows)");
+  if (FMT == wdb::W_E4M3 && inter % 32 != 0)
+    return fail(WD_ERR_SHAPE, "inter must be a multiple of 32 (MXFP8 block size)");
+  if (B == 0) return WD_OK;
+  if (!h || !w || !ids || !scale || !out || (FMT == wdb::W_E4M3 && !wscale))
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(h) || !aligned16(w) || (FMT == wdb::W_E4M3 && !aligned16(wscale)))
+    return fail(WD_ERR_ALIGNMENT, "h and w_down must be 16-byte aligned");
+  if (FMT == wdb::W_E4M3 && ((size_t)E * hidden * (inter / 32)) % 16 != 0)
+    return fail(WD_ERR_ALIGNMENT, "MXFP8 scale tensor size must be a multiple of 16 bytes");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+
+  constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
+  const int grid = std::max(1, std::min(dev->sm_count, hidden / 4));
+  const int rows_max = (hidden + grid - 1) / grid;
+  const int row_bytes = inter * WB;
+  int rs = std::max(1, wdb::DN_STAGE_TARGET / row_bytes);
+  if (rs >= 4) rs -= rs % 4;
+  rs = std::min(rs, rows_max);
+  int stage_bytes = rs * row_bytes + wdb::down_scale_area<FMT>(rs, inter);
+  stage_bytes = ((stage_bytes + 127) / 128) * 128;
+  const int nstages = std::min(8, std::max(2, (96 * 1024) / stage_bytes));
+  // Tokens per launch: routing capacity and the FP32 accumulator tile.
+  int tb = std::max(1, wdb::MAX_SLOTS / topk);
+  tb = std::min(tb, std::max(1, (48 * 1024) / (4 * rows_max)));
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t out_elem = out_fp32 ? 4 : 2;
+  for (int b0 = 0; b0 < B; b0 += tb) {
+    const int bn = std::min(tb, B - b0);
+    const int n = bn * topk;
+    const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
+    const int smem = wdb::down_smem_bytes(nstages, stage_bytes, bn, rows_max, n, E, dedup);
+    if (smem > dev->smem_optin) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    wdb::DownArgs a;
+    a.h = reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter;
+    a.w = w;
+    a.wscale = wscale;
+    a.ids = ids + (size_t)b0 * topk;
+    a.scale = scale + (size_t)b0 * topk;
+    a.out = reinterpret_cast<uint8_t*>(out) + (size_t)b0 * hidden * out_elem;
+    a.out_fp32 = out_fp32 ? 1 : 0;
+    a.status = status;
+    a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+    a.dedup = dedup ? 1 : 0;
+    a.nstages = nstages;
+    a.stage_rows = rs;
+    a.rows_max = rows_max;
+    a.stage_bytes = stage_bytes;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(wdb::DN_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_down_kernel<FMT>, a);
+    if (err != cudaSuccess)
+      return fail(WD_ERR_CUDA, std::string("down launch: ") + cudaGetErrorString(err));
+  }
+  return WD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wd_version(void) { return 100; }
+
+const char* wd_error_string(int err) {
+  switch (err) {
+    case WD_OK: return "ok";
+    case WD_ERR_NULL_POINTER: return "null pointer";
+    case WD_ERR_SHAPE: return "invalid shape";
+    case WD_ERR_ALIGNMENT: return "misaligned pointer";
+    case WD_ERR_UNSUPPORTED: return "unsupported shape";
+    case WD_ERR_CUDA: return "CUDA error";
+    default: return "unknown error";
+  }
+}
+
+const char* wd_last_error_message(void) { return g_last_error.c_str(); }
+
+int wd_moe_gate_up_3d_batched(const void* x, const void* w_gate_up, const int32_t* topk_ids,
+                              void* h_out, int B, int E, int topk, int hidden, int inter,
+                              uint32_t* status, void* stream) {
+  g_last_error.clear();
+  return gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
+                                   topk_ids, h_out, B, E, topk, hidden, inter, status, stream);
+}
+
+int wd_moe_down_3d_batched(const void* h, const void* w_down, const int32_t* topk_ids,
+                           const float* topk_scale, void* y_out, int out_fp32, int B, int E,
+                           int topk, int hidden, int inter, uint32_t* status, void* stream) {
+  g_last_error.clear();
+  return down_impl<wdb::W_BF16>(h, reinterpret_cast<const uint8_t*>(w_down), nullptr, topk_ids,
+                                topk_scale, y_out, out_fp32, B, E, topk, hidden, inter, status,
+                                stream);
+}
+
+int wd_moe_gate_up_3d_batched_mxfp8(const void* x, const uint8_t* w_q, const uint8_t* w_scale,
+                                    const int32_t* topk_ids, void* h_out, int B, int E, int topk,
+                                    int hidden, int inter, uint32_t* status, void* stream) {
+  g_last_error.clear();
+  return gate_up_impl<wdb::W_E4M3>(x, w_q, w_scale, topk_ids, h_out, B, E, topk, hidden, inter,
+                                   status, stream);
+}
+
+int wd_moe_down_3d_batched_mxfp8(const void* h, const uint8_t* w_q, const uint8_t* w_scale,
+                                 const int32_t* topk_ids, const float* topk_scale, void* y_out,
+                                 int out_fp32, int B, int E, int topk, int hidden, int inter,
+                                 uint32_t* status, void* stream) {
+  g_last_error.clear();
+  return down_impl<wdb::W_E4M3>(h, w_q, w_scale, topk_ids, topk_scale, y_out, out_fp32, B, E,
+                                topk, hidden, inter, status, stream);
+}
+
+int wd_status_read(uint32_t* value, int clear) {
+  g_last_error.clear();
+  if (!value) return fail(WD_ERR_NULL_POINTER, "value is NULL");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err == cudaSuccess) err = cudaMemcpyFromSymbol(value, wdb::g_wd_status, sizeof(uint32_t));
+  if (err == cudaSuccess && clear) {
+    const uint32_t zero = 0u;
+    err = cudaMemcpyToSymbol(wdb::g_wd_status, &zero, sizeof(uint32_t));
+  }
+  if (err != cudaSuccess) return fail(WD_ERR_CUDA, std::string("status read: ") + cudaGetErrorString(err));
+  return WD_OK;
+}
+
+}  // extern "C"
