@@ -11,10 +11,12 @@
 //    weight row is streamed from HBM once per call however many tokens of the
 //    batch picked that expert (the reference re-reads it per slot).
 //  * One producer thread streams the gate row and the up row of each item
-//    (chunks of up to 8 KB each) with cp.async.bulk into an NS-deep
-//    shared-memory ring tracked by mbarriers (full: bytes landed, empty:
-//    consumer done).
-//  * Eight consumer warps take whole items round-robin: each lane reads
+//    (chunks of up to 4 KB each, one 8 KB stage per chunk pair) with
+//    cp.async.bulk into shared memory.  Items go to the eight consumer warps
+//    round-robin and every warp owns a private 2-slot ring (16 slots in all,
+//    mbarriers full: bytes landed / empty: consumer done), which it alone
+//    consumes in order.
+//  * Each consumer warp computes its items whole: each lane reads
 //    16-byte weight vectors from shared memory, the matching activation
 //    vectors of every group member from global memory (L1-resident), and
 //    accumulates FP32 dot products; a butterfly reduction and the fused
@@ -41,24 +43,25 @@ struct GateUpArgs {
   uint32_t* status;
   int B, E, K, H, I;
   int dedup;
-  int nstages;
 };
 
 constexpr int GU_CONSUMER_WARPS = 8;
+constexpr int GU_DEPTH = 2;  // ring slots per consumer warp
+constexpr int GU_STAGES = GU_CONSUMER_WARPS * GU_DEPTH;
 constexpr int GU_THREADS = (GU_CONSUMER_WARPS + 1) * 32;
 
 template <int FMT>
 struct GateUpCfg {
   static constexpr int WB = (FMT == W_BF16) ? 2 : 1;        // bytes per weight
-  static constexpr int KC = 8192 / WB;                      // elements per chunk
-  static constexpr int ROW_BYTES = KC * WB;                 // 8 KB
+  static constexpr int KC = 4096 / WB;                      // elements per chunk
+  static constexpr int ROW_BYTES = KC * WB;                 // 4 KB
   static constexpr int SC_BYTES = (FMT == W_E4M3) ? (KC / 32 + 32) : 0;
   static constexpr int STAGE_BYTES = ((2 * ROW_BYTES + 2 * SC_BYTES + 127) / 128) * 128;
 };
 
-__host__ inline int gate_up_smem_bytes(int fmt, int nstages, int n, int E, bool dedup) {
+__host__ inline int gate_up_smem_bytes(int fmt, int n, int E, bool dedup) {
   const int stage = fmt == W_BF16 ? GateUpCfg<W_BF16>::STAGE_BYTES : GateUpCfg<W_E4M3>::STAGE_BYTES;
-  return nstages * stage + 2 * nstages * 8 + 16 + route_smem_bytes(n, E, dedup);
+  return GU_STAGES * stage + 2 * GU_STAGES * 8 + 16 + route_smem_bytes(n, E, dedup);
 }
 
 __device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
@@ -152,16 +155,17 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
   using Cfg = GateUpCfg<FMT>;
   using Math = GateUpMath<FMT>;
   constexpr int KC = Cfg::KC;
+  constexpr int NCW = GU_CONSUMER_WARPS;
+  constexpr int D = GU_DEPTH;
 
   // Let a directly following down kernel start its prologue now.
   pdl_launch_dependents();
 
   extern __shared__ __align__(128) uint8_t smem[];
-  const int NS = a.nstages;
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * Cfg::STAGE_BYTES);
-  uint64_t* empty = full + NS;
-  int* abort_flag = reinterpret_cast<int*>(empty + NS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GU_STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + GU_STAGES;
+  int* abort_flag = reinterpret_cast<int*>(empty + GU_STAGES);
   int* route_base = abort_flag + 4;
 
   const int n = a.B * a.K;
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < GU_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -186,27 +190,36 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
   const int nchunks = (a.H + KC - 1) / KC;
   const size_t H = (size_t)a.H;
 
-  if (warp == GU_CONSUMER_WARPS) {
+  // Item j of this CTA belongs to consumer warp j % NCW.  Every consumer warp
+  // owns D ring slots (slots w*D .. w*D+D-1) that only it consumes, in
+  // order, so a parity wait never runs more than one phase ahead.
+  if (warp == NCW) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int q = 0;
+      int tw[NCW];
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) tw[w] = 0;
       bool ok = true;
-      for (long long t = blockIdx.x; t < items && ok; t += gridDim.x) {
+      int j = 0;
+      for (long long t = blockIdx.x; t < items && ok; t += gridDim.x, ++j) {
         const int sg = (int)(t / a.I);
         const int nn = (int)(t - (long long)sg * a.I);
         const int e = r.sg_exp[sg];
         if (e < 0) continue;
+        const int w = j % NCW;
         const size_t row_g = (size_t)e * 2 * a.I + nn;
         const size_t row_u = row_g + a.I;
-        for (int c = 0; c < nchunks; ++c, ++q) {
+        for (int c = 0; c < nchunks; ++c) {
           const int kc = c * KC;
           const int klen = min(KC, a.H - kc);
-          const int slot = q % NS;
-          const uint32_t ph = (uint32_t)(q / NS) & 1u;
+          const int tt = tw[w]++;
+          const int slot = w * D + tt % D;
+          const uint32_t ph = (uint32_t)(tt / D) & 1u;
           if (!mbar_wait(&empty[slot], ph ^ 1u) || *(volatile int*)abort_flag) {
             *(volatile int*)abort_flag = 1;
             raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            tw[w]--;  // this stage was never issued
             ok = false;
             break;
           }
@@ -237,10 +250,13 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
         }
       }
       // Drain: no copy may still be landing in shared memory when we exit.
-      for (int s = max(0, q - NS); s < q; ++s) {
-        if (!mbar_wait(&full[s % NS], (uint32_t)(s / NS) & 1u)) {
-          raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-          break;
+      for (int w = 0; w < NCW && ok; ++w) {
+        for (int tt = max(0, tw[w] - D); tt < tw[w]; ++tt) {
+          if (!mbar_wait(&full[w * D + tt % D], (uint32_t)(tt / D) & 1u)) {
+            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            ok = false;
+            break;
+          }
         }
       }
     }
@@ -248,25 +264,21 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
   }
 
   // ---------------- consumers ----------------
-  int q = 0;
+  int tt = 0;  // this warp's stage counter
   int j = 0;
   for (long long t = blockIdx.x; t < items; t += gridDim.x, ++j) {
+    if ((j % NCW) != warp) continue;
     const int sg = (int)(t / a.I);
     const int nn = (int)(t - (long long)sg * a.I);
     const int e = r.sg_exp[sg];
-    const bool mine = (j % GU_CONSUMER_WARPS) == warp;
     const int cnt = r.sg_cnt[sg];
     const int beg = r.sg_beg[sg];
     if (e < 0) {
       // Slots with an invalid expert id produce zeros.
-      if (mine && lane < cnt) {
+      if (lane < cnt) {
         const int slot_i = r.members[beg + lane];
         a.out[(size_t)slot_i * a.I + nn] = __float2bfloat16_rn(0.f);
       }
-      continue;
-    }
-    if (!mine) {
-      q += nchunks;
       continue;
     }
     if (*(volatile int*)abort_flag) break;
@@ -282,11 +294,11 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_gate_up_kernel(const GateUp
     for (int m = 0; m < GROUP_MAX; ++m) { ag[m] = 0.f; au[m] = 0.f; }
 
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c, ++q) {
+    for (int c = 0; c < nchunks; ++c, ++tt) {
       const int kc = c * KC;
       const int klen = min(KC, a.H - kc);
-      const int slot = q % NS;
-      if (!mbar_wait(&full[slot], (uint32_t)(q / NS) & 1u)) {
+      const int slot = warp * D + tt % D;
+      if (!mbar_wait(&full[slot], (uint32_t)(tt / D) & 1u)) {
         ok = false;
         break;
       }

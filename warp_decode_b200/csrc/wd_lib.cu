@@ -114,15 +114,13 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
 
-  using Cfg = wdb::GateUpCfg<FMT>;
   const int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
-  int nstages = std::min(6, std::max(2, (96 * 1024) / Cfg::STAGE_BYTES));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
-    const int smem = wdb::gate_up_smem_bytes(FMT, nstages, n, E, dedup);
+    const int smem = wdb::gate_up_smem_bytes(FMT, n, E, dedup);
     if (smem > dev->smem_optin) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
     wdb::GateUpArgs a;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
@@ -133,7 +131,6 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     a.status = status;
     a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
     a.dedup = dedup ? 1 : 0;
-    a.nstages = nstages;
     const long long work = (long long)n * inter;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
