@@ -25,6 +25,7 @@ constexpr uint64_t WD_WAIT_LIMIT_NS = 2000000000ull;
 constexpr int MAX_SLOTS = 512;       // B * topk per launch
 constexpr int MAX_DEDUP_E = 1024;    // experts covered by the dedup table
 constexpr int GROUP_MAX = 8;         // slots per group (register accumulators)
+constexpr int NWARPS = 8;            // compute warps per CTA (both kernels)
 
 // The library-owned status word (one per device context).  The library is
 // built as a single translation unit (wd_lib.cu), so the definition lives here.
@@ -57,6 +58,12 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -120,6 +127,23 @@ __device__ __forceinline__ void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Bulk-copy `bytes` (multiple of 16) from global to shared memory in pieces
+// of at most 16 KB, all completing on `bar` (expect_tx must cover `bytes`).
+__device__ __forceinline__ void bulk_g2s_big(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar, uint64_t policy) {
+  for (uint32_t off = 0; off < bytes; off += 16384u) {
+    const uint32_t len = min(16384u, bytes - off);
+    bulk_g2s(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off, len, bar,
+             policy);
+  }
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // 16-byte read-only global load (activations: L1-cached, re-read by warps).
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
@@ -140,6 +164,26 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& v, float (&f)[8]) {
   f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
 }
 
+// a0 += x[0..3] . w[0..3],  a1 += x[4..7] . w[4..7] for 8 packed bf16 pairs,
+// with Blackwell's mixed-precision FMA (bf16 inputs, FP32 accumulator).  A
+// bf16 widens exactly to FP32 and the product of two bf16 is exact in FP32,
+// so each step equals fmaf() on the widened operands: one rounding per FMA.
+__device__ __forceinline__ void dot8_bf16(float& a0, float& a1, const uint4& x, const uint4& w) {
+  asm("{\n\t"
+      ".reg .b16 x0, x1, x2, x3, x4, x5, x6, x7, w0, w1, w2, w3, w4, w5, w6, w7;\n\t"
+      "mov.b32 {x0, x1}, %2;\n\tmov.b32 {x2, x3}, %3;\n\t"
+      "mov.b32 {x4, x5}, %4;\n\tmov.b32 {x6, x7}, %5;\n\t"
+      "mov.b32 {w0, w1}, %6;\n\tmov.b32 {w2, w3}, %7;\n\t"
+      "mov.b32 {w4, w5}, %8;\n\tmov.b32 {w6, w7}, %9;\n\t"
+      "fma.rn.f32.bf16 %0, x0, w0, %0;\n\tfma.rn.f32.bf16 %1, x4, w4, %1;\n\t"
+      "fma.rn.f32.bf16 %0, x1, w1, %0;\n\tfma.rn.f32.bf16 %1, x5, w5, %1;\n\t"
+      "fma.rn.f32.bf16 %0, x2, w2, %0;\n\tfma.rn.f32.bf16 %1, x6, w6, %1;\n\t"
+      "fma.rn.f32.bf16 %0, x3, w3, %0;\n\tfma.rn.f32.bf16 %1, x7, w7, %1;\n\t"
+      "}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -157,20 +201,23 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
 // Routing groups
 // ---------------------------------------------------------------------------
 // A group is a set of up to GROUP_MAX slots (flat index b*topk+s) routed to
-// the same expert.  Groups are listed in the order of each expert's first
-// appearance in topk_ids, members in increasing slot order, so every CTA of a
-// grid derives the identical list (the kernels split work by group index).
-// An expert id outside [0, E) is mapped to the expert value -1 (such groups
-// are never used to address weights).
+// the same expert.  With dedup, groups are listed in the order of each
+// expert's first appearance in topk_ids, members in increasing slot order, so
+// every CTA of a grid derives the identical list (the kernels split work by
+// group index).  Without dedup every slot is its own group, in slot order.
+// A slot whose expert id is outside [0, E) is always a group of its own with
+// expert -1: kernels stream a valid expert's rows for it (keeping the
+// pipeline uniform) and give it a zero result.
 struct RouteSmem {
   int* ids;      // [n]   expert of each slot (validated, -1 if invalid)
-  int* tab;      // [E+1] dedup table (min slot index, later -(rank+1));
-                 //       entry E collects the invalid ids
-  int* cnt;      // [n]   members per expert group, later exclusive offsets
-  int* gexp;     // [n]   expert of each expert group
-  int* rankpos;  // [n]   rank << 12 | position within group
+  int* tab;      // [E]   dedup table: min slot index, then group rank
+  int* aux;      // [n]   scratch
+  int* rank;     // [n]   group rank of each slot
+  int* gcnt;     // [n]   members per group
+  int* goff;     // [n]   first member index of each group
   int* members;  // [n]   slots ordered by (group, slot)
-  int* sg_exp;   // [n]   expert of each capped group (or -1)
+  int* mtok;     // [n]   token (slot / topk) of each entry of `members`
+  int* sg_exp;   // [n]   expert of each capped group (-1: invalid slot)
   int* sg_beg;   // [n]   first member (index into members) of each capped group
   int* sg_cnt;   // [n]   member count of each capped group
   int* nsg;      // [1]   number of capped groups
@@ -178,129 +225,166 @@ struct RouteSmem {
 
 // Shared-memory bytes needed by RouteSmem for n slots and E experts.
 __host__ __device__ inline int route_smem_bytes(int n, int E, bool dedup) {
-  int ints = 9 * n + 1 + (dedup ? E + 1 : 0);
+  int ints = 11 * n + 1 + (dedup ? E : 0);
   return ((ints * 4 + 127) / 128) * 128;
 }
 
 __device__ inline RouteSmem route_carve(int* base, int n, int E, bool dedup) {
   RouteSmem r;
-  r.ids = base;
-  r.cnt = r.ids + n;
-  r.gexp = r.cnt + n;
-  r.rankpos = r.gexp + n;
-  r.members = r.rankpos + n;
-  r.sg_exp = r.members + n;
-  r.sg_beg = r.sg_exp + n;
-  r.sg_cnt = r.sg_beg + n;
-  r.nsg = r.sg_cnt + n;
-  r.tab = dedup ? r.nsg + 1 : nullptr;
+  int* p = base;
+  r.ids = p; p += n;
+  r.aux = p; p += n;
+  r.rank = p; p += n;
+  r.gcnt = p; p += n;
+  r.goff = p; p += n;
+  r.members = p; p += n;
+  r.mtok = p; p += n;
+  r.sg_exp = p; p += n;
+  r.sg_beg = p; p += n;
+  r.sg_cnt = p; p += n;
+  r.nsg = p; p += 1;
+  r.tab = dedup ? p : nullptr;
   return r;
 }
 
-// Build the groups for slots [0, n) of `topk_ids` (a device pointer).
-// Must be called by all threads of the CTA; ends with __syncthreads().
-// dedup = false makes every slot its own group (no table, no scans).
-__device__ inline void build_groups(const RouteSmem& r, const int32_t* __restrict__ topk_ids,
-                                    int n, int E, bool dedup, uint32_t* status) {
-  const int tid = threadIdx.x;
-  const int nthreads = blockDim.x;
+// Exclusive prefix sum of a[0..cnt) in place by one warp (lanes in step);
+// returns the total.  cnt <= MAX_SLOTS.
+__device__ __forceinline__ int warp_exclusive_scan(int* a, int cnt, int lane) {
+  int base = 0;
+  for (int c = 0; c < cnt; c += 32) {
+    const int i = c + lane;
+    const int v = i < cnt ? a[i] : 0;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    if (i < cnt) a[i] = base + inc - v;
+    base += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  return base;
+}
+
+// Load and validate this launch's topk_ids into shared memory.  All threads.
+// Ends with __syncthreads().
+__device__ inline void load_ids(const RouteSmem& r, const int32_t* __restrict__ topk_ids, int n,
+                                int E, uint32_t* status) {
   bool bad = false;
-  for (int i = tid; i < n; i += nthreads) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
     int e = __ldg(topk_ids + i);
     if (e < 0 || e >= E) { e = -1; bad = true; }
     r.ids[i] = e;
   }
-  if (__syncthreads_or(bad) && tid == 0) raise_status(status, WD_STATUS_BAD_EXPERT_ID);
+  if (__syncthreads_or(bad) && threadIdx.x == 0) raise_status(status, WD_STATUS_BAD_EXPERT_ID);
+}
 
+// Build the capped groups from r.ids (see load_ids).  All threads; ends with
+// __syncthreads().
+__device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, bool dedup) {
+  const int tid = threadIdx.x;
+  const int nt = blockDim.x;
+  const int lane = tid & 31;
   if (!dedup) {
-    for (int i = tid; i < n; i += nthreads) {
-      r.members[i] = i;
+    for (int i = tid; i < n; i += nt) {
       r.sg_exp[i] = r.ids[i];
       r.sg_beg[i] = i;
       r.sg_cnt[i] = 1;
+      r.members[i] = i;
+      r.mtok[i] = i / K;
     }
     if (tid == 0) *r.nsg = n;
     __syncthreads();
     return;
   }
-
-  // Invalid ids all go to one pseudo-expert E (table slot E).
-  for (int e = tid; e <= E; e += nthreads) r.tab[e] = 0x7fffffff;
-  for (int i = tid; i < n; i += nthreads) r.cnt[i] = 0;
+  __shared__ int s_groups;
+  for (int e = tid; e < E; e += nt) r.tab[e] = 0x7fffffff;
+  for (int i = tid; i < n; i += nt) r.gcnt[i] = 0;
   __syncthreads();
-  for (int i = tid; i < n; i += nthreads) {
+  for (int i = tid; i < n; i += nt) {
     const int e = r.ids[i];
-    atomicMin(&r.tab[e < 0 ? E : e], i);
+    if (e >= 0) atomicMin(&r.tab[e], i);
   }
   __syncthreads();
-
-  // One warp walks the slots in order: assign group ranks (order of first
-  // appearance) and each slot's position inside its group.  Deterministic.
+  // A group opens at the first slot of each expert and at every invalid slot.
+  for (int i = tid; i < n; i += nt) {
+    const int e = r.ids[i];
+    const int open = (e < 0 || r.tab[e] == i) ? 1 : 0;
+    r.aux[i] = open;
+    r.rank[i] = open;
+  }
+  __syncthreads();
   if (tid < 32) {
-    const int lane = tid;
-    const unsigned lt = (1u << lane) - 1u;
-    int base = 0;
-    for (int c = 0; c < n; c += 32) {
-      const int i = c + lane;
-      const bool valid = i < n;
-      const int e = valid ? r.ids[i] : 0;
-      const int key = e < 0 ? E : e;
-      const int t = valid ? r.tab[key] : 0;
-      const bool first = valid && (t == i);
-      const unsigned fb = __ballot_sync(0xffffffffu, first);
-      int rank = base + __popc(fb & lt);
-      // Non-first slot: its group was opened earlier (t < 0 after rewrite),
-      // or by a lane of this same chunk (t = that lane's slot index).
-      const int src_lane = (valid && t >= 0) ? (t - c) : lane;
-      const int lane_rank = __shfl_sync(0xffffffffu, rank, src_lane & 31);
-      if (valid && !first) rank = (t < 0) ? (-t - 1) : lane_rank;
-      // Position inside the group: earlier chunks (cnt) + earlier lanes here.
-      const unsigned same = __match_any_sync(0xffffffffu, valid ? rank : -1);
-      const int pos = valid ? (r.cnt[rank] + __popc(same & lt)) : 0;
-      __syncwarp();
-      if (valid) {
-        r.rankpos[i] = (rank << 12) | pos;
-        if ((same & lt) == 0u) r.cnt[rank] += __popc(same);
-        if (first) { r.tab[key] = -(rank + 1); r.gexp[rank] = e; }
-      }
-      __syncwarp();
-      base += __popc(fb);
-    }
-    // Exclusive offsets of expert groups and the capped-group list.
-    int off = 0, sg = 0;
-    for (int c = 0; c < base; c += 32) {
-      const int g = c + lane;
-      const int cnt = g < base ? r.cnt[g] : 0;
-      const int nsub = (cnt + GROUP_MAX - 1) / GROUP_MAX;
-      int inc_cnt = cnt, inc_sub = nsub;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int a = __shfl_up_sync(0xffffffffu, inc_cnt, o);
-        const int b = __shfl_up_sync(0xffffffffu, inc_sub, o);
-        if (lane >= o) { inc_cnt += a; inc_sub += b; }
-      }
-      const int my_off = off + inc_cnt - cnt;
-      const int my_sg = sg + inc_sub - nsub;
-      if (g < base) {
-        r.cnt[g] = my_off;  // now the exclusive member offset of group g
-        const int e = r.gexp[g];
-        for (int j = 0; j < nsub; ++j) {
-          r.sg_exp[my_sg + j] = e;
-          r.sg_beg[my_sg + j] = my_off + j * GROUP_MAX;
-          r.sg_cnt[my_sg + j] = min(GROUP_MAX, cnt - j * GROUP_MAX);
-        }
-      }
-      off += __shfl_sync(0xffffffffu, inc_cnt, 31);
-      sg += __shfl_sync(0xffffffffu, inc_sub, 31);
-    }
-    if (lane == 0) *r.nsg = sg;
+    const int groups = warp_exclusive_scan(r.rank, n, lane);  // rank of opening slots
+    if (lane == 0) s_groups = groups;
   }
   __syncthreads();
-  for (int i = tid; i < n; i += nthreads) {
-    const int rp = r.rankpos[i];
-    r.members[r.cnt[rp >> 12] + (rp & 0xfff)] = i;
+  for (int i = tid; i < n; i += nt) {
+    if (r.aux[i]) {
+      const int e = r.ids[i];
+      if (e >= 0) r.tab[e] = r.rank[i];
+    }
   }
   __syncthreads();
+  // Every slot learns its group; counts and (unordered) positions by atomics.
+  for (int i = tid; i < n; i += nt) {
+    const int e = r.ids[i];
+    const int g = (e < 0) ? r.rank[i] : r.tab[e];
+    r.rank[i] = g;
+    r.aux[i] = atomicAdd(&r.gcnt[g], 1);
+  }
+  __syncthreads();
+  const int groups = s_groups;
+  if (tid < 32) {
+    for (int g = lane; g < groups; g += 32) r.goff[g] = r.gcnt[g];
+    __syncwarp();
+    warp_exclusive_scan(r.goff, groups, lane);
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += nt) r.members[r.goff[r.rank[i]] + r.aux[i]] = i;
+  __syncthreads();
+  // Members in slot order (groups are small: insertion sort per group), and
+  // the number of capped groups per group.
+  for (int g = tid; g < groups; g += nt) {
+    const int b = r.goff[g], c = r.gcnt[g];
+    for (int x = b + 1; x < b + c; ++x) {
+      const int v = r.members[x];
+      int y = x - 1;
+      while (y >= b && r.members[y] > v) { r.members[y + 1] = r.members[y]; --y; }
+      r.members[y + 1] = v;
+    }
+    r.aux[g] = (c + GROUP_MAX - 1) / GROUP_MAX;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const int total = warp_exclusive_scan(r.aux, groups, lane);
+    if (lane == 0) *r.nsg = total;
+  }
+  __syncthreads();
+  for (int g = tid; g < groups; g += nt) {
+    const int b = r.goff[g], c = r.gcnt[g], s0 = r.aux[g];
+    const int e = r.ids[r.members[b]];
+    for (int j = 0; j * GROUP_MAX < c; ++j) {
+      r.sg_exp[s0 + j] = e;
+      r.sg_beg[s0 + j] = b + j * GROUP_MAX;
+      r.sg_cnt[s0 + j] = min(GROUP_MAX, c - j * GROUP_MAX);
+    }
+  }
+  for (int i = tid; i < n; i += nt) r.mtok[i] = r.members[i] / K;
+  __syncthreads();
+}
+
+// Non-blocking mbarrier phase test.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
 }  // namespace wdb

@@ -60,7 +60,10 @@ int device_info(DeviceInfo** out) {
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
-      err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin);
+      // Dynamic + static shared memory must fit the opt-in limit; the kernels
+      // use well under 1 KB of static shared memory.
+      err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 d.smem_optin - 1024);
       // Full shared-memory carve-out so a gate_up CTA and an early-started
       // down CTA fit on one SM together.
       if (err == cudaSuccess)
@@ -114,14 +117,31 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
 
+  constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
   const int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
+  if ((long long)std::min(tb, B) * topk * inter >= (1LL << 31))
+    return fail(WD_ERR_UNSUPPORTED, "B*topk*inter per launch must be < 2^31");
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
-    const int smem = wdb::gate_up_smem_bytes(FMT, n, E, dedup);
-    if (smem > dev->smem_optin) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    // Ring: 8 warps x 2 slots of (gate, up) row chunks of 4 KB each (128 KB),
+    // halved when x would not fit next to it; x staged if it fits in 128 KB.
+    const int route = wdb::route_smem_bytes(n, E, dedup);
+    const long long x_bytes = (long long)bn * hidden * 2;
+    int kc = 4096 / WB;
+    int depth = 2;
+    bool x_smem = x_bytes <= 128 * 1024;
+    auto need = [&]() {
+      return wdb::gate_up_smem_bytes(depth, wdb::gate_up_stage_bytes(FMT, kc),
+                                     x_smem ? (int)x_bytes : 0, n, E, dedup);
+    };
+    const int budget = dev->smem_optin - 2048;
+    if (need() > budget) kc /= 2;
+    if (need() > budget) x_smem = false;
+    if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    (void)route;
     wdb::GateUpArgs a;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
     a.w = w;
@@ -131,11 +151,15 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     a.status = status;
     a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
     a.dedup = dedup ? 1 : 0;
+    a.kc = kc;
+    a.depth = depth;
+    a.stage_bytes = wdb::gate_up_stage_bytes(FMT, kc);
+    a.x_smem = x_smem ? 1 : 0;
     const long long work = (long long)n * inter;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
     cfg.blockDim = dim3(wdb::GU_THREADS);
-    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.dynamicSmemBytes = (size_t)need();
     cfg.stream = s;
     cfg.attrs = nullptr;
     cfg.numAttrs = 0;
@@ -167,18 +191,23 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
   if ((rc = device_info(&dev))) return rc;
 
   constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
+  constexpr int EPV = FMT == wdb::W_BF16 ? 8 : 16;
   const int grid = std::max(1, std::min(dev->sm_count, hidden / 4));
   const int rows_max = (hidden + grid - 1) / grid;
   const int row_bytes = inter * WB;
-  int rs = std::max(1, wdb::DN_STAGE_TARGET / row_bytes);
-  if (rs >= 4) rs -= rs % 4;
-  rs = std::min(rs, rows_max);
-  int stage_bytes = rs * row_bytes + wdb::down_scale_area<FMT>(rs, inter);
+  // Item = chunk of >= 4 KB of contiguous rows (smaller bulk copies do not
+  // saturate HBM), chunks of one CTA's block as even as that allows.
+  const int rc_min = std::min(rows_max, std::max(1, (4096 + row_bytes - 1) / row_bytes));
+  const int nch = std::max(1, rows_max / rc_min);
+  const int rows_chunk = (rows_max + nch - 1) / nch;
+  const int nvec = inter / EPV;
+  const int lpr = nvec <= 32 ? 8 : (nvec <= 64 ? 16 : 32);
+  int stage_bytes = rows_chunk * row_bytes + wdb::down_scale_area<FMT>(rows_chunk, inter);
   stage_bytes = ((stage_bytes + 127) / 128) * 128;
-  const int nstages = std::min(8, std::max(2, (96 * 1024) / stage_bytes));
-  // Tokens per launch: routing capacity and the FP32 accumulator tile.
+  const int depth = std::min(4, std::max(2, (96 * 1024) / (wdb::NWARPS * stage_bytes)));
+  // Tokens per launch: routing capacity and the 8 per-warp FP32 tiles.
   int tb = std::max(1, wdb::MAX_SLOTS / topk);
-  tb = std::min(tb, std::max(1, (48 * 1024) / (4 * rows_max)));
+  tb = std::min(tb, std::max(1, (64 * 1024) / (4 * wdb::NWARPS * rows_max)));
 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -189,8 +218,15 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
-    const int smem = wdb::down_smem_bytes(nstages, stage_bytes, bn, rows_max, n, E, dedup);
-    if (smem > dev->smem_optin) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    const long long h_bytes = (long long)n * inter * 2;
+    bool h_smem = h_bytes <= 64 * 1024;
+    auto need = [&]() {
+      return wdb::down_smem_bytes(depth, stage_bytes, h_smem ? (int)h_bytes : 0, bn, rows_max, n,
+                                  E, dedup);
+    };
+    const int budget = dev->smem_optin - 2048;
+    if (need() > budget) h_smem = false;
+    if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
     wdb::DownArgs a;
     a.h = reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter;
     a.w = w;
@@ -202,14 +238,16 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
     a.status = status;
     a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
     a.dedup = dedup ? 1 : 0;
-    a.nstages = nstages;
-    a.stage_rows = rs;
-    a.rows_max = rows_max;
+    a.depth = depth;
+    a.rc = rows_chunk;
+    a.lpr = lpr;
     a.stage_bytes = stage_bytes;
+    a.rows_max = rows_max;
+    a.h_smem = h_smem ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(wdb::DN_THREADS);
-    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.dynamicSmemBytes = (size_t)need();
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
