@@ -26,6 +26,10 @@ constexpr int MAX_SLOTS = 512;       // B * topk per launch
 constexpr int MAX_DEDUP_E = 1024;    // experts covered by the dedup table
 constexpr int GROUP_MAX = 8;         // slots per group (register accumulators)
 constexpr int NWARPS = 8;            // compute warps per CTA (both kernels)
+#ifndef WD_GU_DEPTH
+#define WD_GU_DEPTH 2
+#endif
+constexpr int GU_DEPTH_MAX = WD_GU_DEPTH;  // gate_up ring slots per consumer warp
 
 // The library-owned status word (one per device context).  The library is
 // built as a single translation unit (wd_lib.cu), so the definition lives here.

@@ -70,7 +70,7 @@ template <int FMT, int MAXM>
 __device__ __forceinline__ void dn_row(const uint8_t* __restrict__ wrow, const uint8_t* srow,
                                        int nvec, int lj, int lpr,
                                        const __nv_bfloat16* const (&hr)[GROUP_MAX], bool hsm,
-                                       int cnt, float (&acc)[GROUP_MAX], float (&acc2)[GROUP_MAX]) {
+                                       int cnt, float (&acc)[MAXM], float (&acc2)[MAXM]) {
   if constexpr (FMT == W_BF16) {
 #pragma unroll 2
     for (int v = lj; v < nvec; v += lpr) {
@@ -126,24 +126,46 @@ __device__ __forceinline__ void dn_item(const uint8_t* __restrict__ st, const ui
     sc[m] = s_scale[slot_i];
     tok[m] = r.mtok[at];
   }
-  for (int rb = 0; rb < nr; rb += rpp) {
-    const int row = rb + prow;  // row within the chunk
-    const bool active = row < nr;
-    float acc[GROUP_MAX], acc2[GROUP_MAX];
+  // A lane's rows of the item are prow, prow + rpp, ...; up to DN_ROWS of
+  // them are computed together so their load/FMA/shuffle chains overlap.
+  constexpr int DN_ROWS = MAXM <= 2 ? 4 : (MAXM <= 4 ? 2 : 1);
+  for (int rb = 0; rb < nr; rb += DN_ROWS * rpp) {
+    float acc[DN_ROWS][MAXM], acc2[DN_ROWS][MAXM];
 #pragma unroll
-    for (int m = 0; m < MAXM; ++m) { acc[m] = 0.f; acc2[m] = 0.f; }
-    if (active)
-      dn_row<FMT, MAXM>(st + (size_t)row * row_bytes,
-                        FMT == W_E4M3 ? sbase + (size_t)row * sc_row : nullptr, nvec, lj, lpr, hr,
-                        hsm, cnt, acc, acc2);
+    for (int q = 0; q < DN_ROWS; ++q)
 #pragma unroll
-    for (int m = 0; m < MAXM; ++m) {
-      if (m < cnt) {
-        float v = acc[m] + acc2[m];
-        for (int o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (active && lj == 0) {
-          float* dst = &my_tile[tok[m] * rows_max + lr0 + row];
-          *dst = fmaf(sc[m], v, *dst);
+      for (int m = 0; m < MAXM; ++m) { acc[q][m] = 0.f; acc2[q][m] = 0.f; }
+#pragma unroll
+    for (int q = 0; q < DN_ROWS; ++q) {
+      const int row = rb + q * rpp + prow;
+      if (row < nr)
+        dn_row<FMT, MAXM>(st + (size_t)row * row_bytes,
+                          FMT == W_E4M3 ? sbase + (size_t)row * sc_row : nullptr, nvec, lj, lpr,
+                          hr, hsm, cnt, acc[q], acc2[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < DN_ROWS; ++q)
+#pragma unroll
+      for (int m = 0; m < MAXM; ++m) acc[q][m] += acc2[q][m];
+    for (int o = lpr >> 1; o > 0; o >>= 1) {
+#pragma unroll
+      for (int q = 0; q < DN_ROWS; ++q)
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m)
+          if (m < cnt) acc[q][m] += __shfl_xor_sync(0xffffffffu, acc[q][m], o);
+    }
+    if (lj == 0) {
+#pragma unroll
+      for (int q = 0; q < DN_ROWS; ++q) {
+        const int row = rb + q * rpp + prow;
+        if (row < nr) {
+#pragma unroll
+          for (int m = 0; m < MAXM; ++m) {
+            if (m < cnt) {
+              float* dst = &my_tile[tok[m] * rows_max + lr0 + row];
+              *dst = fmaf(sc[m], acc[q][m], *dst);
+            }
+          }
         }
       }
     }

@@ -126,22 +126,28 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
-    // Ring: 8 warps x 2 slots of (gate, up) row chunks of 4 KB each (128 KB),
-    // halved when x would not fit next to it; x staged if it fits in 128 KB.
-    const int route = wdb::route_smem_bytes(n, E, dedup);
+    // Ring: 8 warps x `depth` slots of (gate, up) row chunks of 4 KB each; x
+    // staged in shared memory if it fits in 128 KB.  Preference order: a
+    // deep ring (at B=1 a CTA's whole share, ~170 KB, is then requested at
+    // once: one copy latency instead of two), then x staged, then 2 KB
+    // chunks, then x read from L2.
     const long long x_bytes = (long long)bn * hidden * 2;
-    int kc = 4096 / WB;
-    int depth = 2;
-    bool x_smem = x_bytes <= 128 * 1024;
-    auto need = [&]() {
-      return wdb::gate_up_smem_bytes(depth, wdb::gate_up_stage_bytes(FMT, kc),
-                                     x_smem ? (int)x_bytes : 0, n, E, dedup);
-    };
+    const bool x_fits = x_bytes <= 128 * 1024;
     const int budget = dev->smem_optin - 2048;
-    if (need() > budget) kc /= 2;
-    if (need() > budget) x_smem = false;
-    if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
-    (void)route;
+    struct Choice { int depth, kc; bool x_smem; };
+    const Choice choices[] = {{wdb::GU_DEPTH_MAX, 4096 / WB, x_fits}, {2, 4096 / WB, x_fits},
+                              {2, 2048 / WB, x_fits}, {2, 2048 / WB, false}};
+    int kc = 0, depth = 0, smem = 0;
+    bool x_smem = false;
+    for (const Choice& c : choices) {
+      const int need = wdb::gate_up_smem_bytes(c.depth, wdb::gate_up_stage_bytes(FMT, c.kc),
+                                               c.x_smem ? (int)x_bytes : 0, n, E, dedup);
+      if (need <= budget) {
+        kc = c.kc; depth = c.depth; x_smem = c.x_smem; smem = need;
+        break;
+      }
+    }
+    if (!smem) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
     wdb::GateUpArgs a;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
     a.w = w;
@@ -159,7 +165,7 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
     cfg.blockDim = dim3(wdb::GU_THREADS);
-    cfg.dynamicSmemBytes = (size_t)need();
+    cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
     cfg.attrs = nullptr;
     cfg.numAttrs = 0;
