@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 8, names
+    assert len(names) == 9, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -23,6 +23,14 @@ def test_library_exports_every_header_symbol():
                          text=True, check=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
     assert exported == set(names), exported ^ set(names)
+
+
+def test_gate_up_path_selector_validates():
+    L = capi.lib()
+    assert L.wd_set_gate_up_path(3) == capi.WD_ERR_SHAPE
+    assert b"path" in L.wd_last_error_message()
+    for p in (capi.GATE_UP_SIMT, capi.GATE_UP_TC, capi.GATE_UP_AUTO):
+        assert L.wd_set_gate_up_path(p) == capi.WD_OK
 
 
 def test_version_and_error_strings():

@@ -179,6 +179,8 @@ int64_t status(bool clear, int64_t device) {
   return static_cast<int64_t>(v);
 }
 
+void set_gate_up_path(int64_t path) { check_rc(wd_set_gate_up_path(static_cast<int>(path))); }
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -201,4 +203,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B") = py::none(), py::arg("fp32_out") = false);
   m.def("status", &status, "Read (and clear) the device status word of the library",
         py::arg("clear") = true, py::arg("device") = 0);
+  m.def("set_gate_up_path", &set_gate_up_path,
+        "gate_up kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
+        py::arg("path"));
 }

@@ -285,7 +285,8 @@ __device__ inline void load_ids(const RouteSmem& r, const int32_t* __restrict__ 
 
 // Build the capped groups from r.ids (see load_ids).  All threads; ends with
 // __syncthreads().
-__device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, bool dedup) {
+__device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, bool dedup,
+                                    int cap = GROUP_MAX) {
   const int tid = threadIdx.x;
   const int nt = blockDim.x;
   const int lane = tid & 31;
@@ -357,7 +358,7 @@ __device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, boo
       while (y >= b && r.members[y] > v) { r.members[y + 1] = r.members[y]; --y; }
       r.members[y + 1] = v;
     }
-    r.aux[g] = (c + GROUP_MAX - 1) / GROUP_MAX;
+    r.aux[g] = (c + cap - 1) / cap;
   }
   __syncthreads();
   if (tid < 32) {
@@ -368,10 +369,10 @@ __device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, boo
   for (int g = tid; g < groups; g += nt) {
     const int b = r.goff[g], c = r.gcnt[g], s0 = r.aux[g];
     const int e = r.ids[r.members[b]];
-    for (int j = 0; j * GROUP_MAX < c; ++j) {
+    for (int j = 0; j * cap < c; ++j) {
       r.sg_exp[s0 + j] = e;
-      r.sg_beg[s0 + j] = b + j * GROUP_MAX;
-      r.sg_cnt[s0 + j] = min(GROUP_MAX, c - j * GROUP_MAX);
+      r.sg_beg[s0 + j] = b + j * cap;
+      r.sg_cnt[s0 + j] = min(cap, c - j * cap);
     }
   }
   for (int i = tid; i < n; i += nt) r.mtok[i] = r.members[i] / K;

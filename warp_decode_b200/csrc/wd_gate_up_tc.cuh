@@ -1,0 +1,294 @@
+// gate_up projection + SiLU on the 5th-generation tensor cores (tcgen05),
+// sm_100a.  Same operation and output as moe_gate_up_kernel
+// (csrc/moe_gate_up_3d_batched.cu:14-115 of the reference):
+//   h[slot, i] = silu(x[tok] . Wgu[e, i, :]) * (x[tok] . Wgu[e, I + i, :]).
+//
+// Design (B200):
+//  * Work item = (expert, tile of 64 neurons).  A group is every routed slot
+//    of one expert, so each expert's weights cross HBM once per call.
+//  * The A operand is 128 weight rows, gate rows [i0, i0+64) then the
+//    matching up rows, fetched by ONE 4-D TMA box over the view
+//    (k, neuron, gate|up, expert) of w_gate_up [E, 2I, H]; neurons past I
+//    are zero-filled by the TMA unit.  TMEM lane i then holds gate (i < 64)
+//    or up (i >= 64) of neuron i0 + (i & 63); the epilogue pairs them
+//    through a 2 KB shared-memory exchange.
+//  * The B operand is every token of the launch (N = B rounded up to 16,
+//    at most 64; rows past B zero-filled), one 2-D TMA box per K stage.
+//    The MMA computes all B columns; the epilogue reads only the columns of
+//    the group's tokens.  Tensor-core time is far below the weight stream at
+//    these N, and x (B x 8 KB) stays in L2.
+//  * Warp roles: warp 0 = TMA producer (ring of `stages` stages of `kch`
+//    64-wide K chunks: 16 KB of weights + B x 128 B of x per chunk),
+//    warp 1 = TMEM allocator + single-thread MMA issuer (4 x K=16 MMAs per
+//    64-wide K stage, tcgen05.commit releases the stage), warps 2-5 =
+//    epilogue (tcgen05.ld, silu(g) * u, bf16 store).  Two TMEM accumulator
+//    buffers let the epilogue of one item overlap the MMAs of the next.
+//  * Every wait is bounded; on timeout the CTA raises WD_STATUS_WAIT_TIMEOUT,
+//    stops, lets its in-flight copies and MMAs land, frees TMEM and returns.
+#pragma once
+
+#include "wd_gate_up.cuh"
+#include "wd_tc.cuh"
+
+namespace wdb {
+
+constexpr int TC_M = 128;                     // weight rows per tile (64 gate + 64 up)
+constexpr int TC_NEUR = 64;                   // neurons per tile
+constexpr int TC_BK = 64;                     // K elements per stage (128-byte rows)
+constexpr int TC_NMAX = 64;                   // tokens per launch (max MMA N)
+constexpr int TC_A_BYTES = TC_M * TC_BK * 2;  // 16 KB
+constexpr int TC_THREADS = 6 * 32;
+constexpr int TC_TMEM_COLS = 2 * TC_NMAX;     // two fp32 accumulator buffers
+
+struct GateUpTcArgs {
+  const int32_t* ids;   // [B, K]
+  __nv_bfloat16* out;   // [B*K, I]
+  uint32_t* status;
+  int B, E, K, H, I;
+  int stages;           // smem ring depth
+  int npad;             // MMA N: B rounded up to 16 (<= TC_NMAX)
+  int kch;              // 64-wide K chunks per stage
+};
+
+constexpr int TC_XCH = 8;                     // members per epilogue exchange round
+
+// One stage: kch A chunks (16 KB each) then kch B chunks (npad rows x 128 B).
+__host__ __device__ inline int gate_up_tc_stage_bytes(int kch, int npad) {
+  return kch * (TC_A_BYTES + npad * TC_BK * 2);
+}
+
+__host__ inline int gate_up_tc_smem_bytes(int stages, int kch, int npad, int n, int E) {
+  return 1024 + stages * gate_up_tc_stage_bytes(kch, npad) + TC_XCH * TC_NEUR * 4 +
+         (2 * stages + 5) * 8 + 16 + CTRL_INTS * 4 + route_smem_bytes(n, E, true);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    moe_gate_up_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                          const __grid_constant__ CUtensorMap tm_x, const GateUpTcArgs a) {
+  pdl_launch_dependents();
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* base = smem_raw + pad;
+  const int S = a.stages;
+  const int KCH = a.kch;
+  const int BT = a.npad * TC_BK * 2;  // bytes of one B chunk
+  const int SB = gate_up_tc_stage_bytes(KCH, a.npad);
+  uint8_t* ring = base;
+  float* xch = reinterpret_cast<float*>(ring + (size_t)S * SB);  // [TC_XCH][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xch + TC_XCH * TC_NEUR);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;  // [2] accumulator drained
+  uint64_t* done = tempty + 2;   // MMA drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* ctrl = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
+
+  const int n = a.B * a.K;
+  const RouteSmem r = route_carve(route_base, n, a.E, true);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull[0], 1);
+    mbar_init(&tfull[1], 1);
+    mbar_init(&tempty[0], 4);
+    mbar_init(&tempty[1], 4);
+    mbar_init(done, 1);
+    ctrl[0] = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  load_ids(r, a.ids, n, a.E, a.status);           // ends with __syncthreads
+  build_groups(r, n, a.E, a.K, true, MAX_SLOTS);  // ends with __syncthreads
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_tiles = (a.I + TC_NEUR - 1) / TC_NEUR;
+  const int items = *r.nsg * n_tiles;
+  const int nkc = (a.H + TC_BK - 1) / TC_BK;  // 64-wide K chunks
+  const int nk = (nkc + KCH - 1) / KCH;        // stages per item
+  const int G = (int)gridDim.x;
+
+  // Bounded wait that also gives up once another role has aborted.
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((it & 31u) == 0) {
+        if (ctrl[0]) return false;
+        if (globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+          raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+          ctrl[0] = 1;
+          return false;
+        }
+      }
+    }
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_x = l2_policy_evict_last();
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = (int)blockIdx.x; ok && t < items; t += G) {
+      const int g = t / n_tiles, mt = t - g * n_tiles;
+      const int e = r.sg_exp[g];
+      if (e < 0) continue;
+      for (int ks = 0; ks < nk; ++ks, ++it) {
+        const int slot = (int)(it % (uint32_t)S);
+        const uint32_t ph = (it / (uint32_t)S) & 1u;
+        if (lane == 0) {
+          if (!wait(&empty[slot], ph ^ 1u)) {
+            ok = false;
+          } else {
+            const int c0 = ks * KCH, nc = min(KCH, nkc - c0);
+            uint8_t* st = ring + (size_t)slot * SB;
+            mbar_arrive_expect_tx(&full[slot], (uint32_t)nc * (TC_A_BYTES + BT));
+            for (int c = 0; c < nc; ++c)
+              tma_load_4d(st + c * TC_A_BYTES, &tm_w, (c0 + c) * TC_BK, mt * TC_NEUR, 0, e,
+                          &full[slot], pol_w);
+            for (int c = 0; c < nc; ++c)
+              tma_load_2d(st + KCH * TC_A_BYTES + c * BT, &tm_x, (c0 + c) * TC_BK, 0, &full[slot],
+                          pol_x);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
+    }
+    // After an abort let every issued copy land before the CTA can exit.
+    if (!ok && lane == 0) {
+      const uint32_t lo = it > (uint32_t)S ? it - (uint32_t)S : 0u;
+      for (uint32_t i = lo; i < it; ++i) {
+        uint64_t* bar = &full[i % (uint32_t)S];
+        const uint32_t ph = (i / (uint32_t)S) & 1u;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t0 < WD_WAIT_LIMIT_NS) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one thread) ----------------
+    if (lane == 0) {
+      uint32_t it = 0, vi = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = (int)blockIdx.x; ok && t < items; t += G) {
+        const int g = t / n_tiles;
+        if (r.sg_exp[g] < 0) continue;
+        const uint32_t buf = vi & 1u;
+        if (!wait(&tempty[buf], ((vi >> 1) & 1u) ^ 1u)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t idesc = tc_idesc_bf16(TC_M, a.npad);
+        const uint32_t d = tmem + buf * TC_NMAX;
+        for (int ks = 0; ks < nk; ++ks, ++it) {
+          const int slot = (int)(it % (uint32_t)S);
+          if (!wait(&full[slot], (it / (uint32_t)S) & 1u)) { ok = false; break; }
+          tc_fence_after();
+          const uint8_t* st = ring + (size_t)slot * SB;
+          const int nc = min(KCH, nkc - ks * KCH);
+          for (int c = 0; c < nc; ++c) {
+            const uint64_t ad = tc_desc_sw128(smem_u32(st + c * TC_A_BYTES));
+            const uint64_t bd = tc_desc_sw128(smem_u32(st + KCH * TC_A_BYTES + c * BT));
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; ++kk)
+              tc_mma_bf16(d, ad + 2u * kk, bd + 2u * kk, idesc, (ks | c | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[slot]);
+          issued = true;
+        }
+        if (!ok) break;
+        tc_commit(&tfull[buf]);
+        ++vi;
+      }
+      // Every MMA this thread issued has completed before TMEM is freed.
+      if (issued) {
+        tc_commit(done);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(done, 0) && globaltimer_ns() - t0 < WD_WAIT_LIMIT_NS) {
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: warps 2..5, TMEM lane quarter warp % 4 -----
+    // Quarters 0, 1 read gate rows (neurons 32q + lane), quarters 2, 3 the
+    // up rows of the same neurons; up values cross over in `xch`.
+    const int q = warp & 3;
+    const bool is_gate = q < 2;
+    const int I = a.I;
+    uint32_t vi = 0;
+    for (int t = (int)blockIdx.x; t < items; t += G) {
+      const int g = t / n_tiles, mt = t - g * n_tiles;
+      const int e = r.sg_exp[g];
+      const int cnt = r.sg_cnt[g], beg = r.sg_beg[g];
+      const int nn = mt * TC_NEUR + 32 * (q & 1) + lane;
+      if (e < 0) {
+        // A slot with an out-of-range expert id yields zeros.
+        if (is_gate && nn < I)
+          for (int c = 0; c < cnt; ++c)
+            a.out[(size_t)r.members[beg + c] * I + nn] = __float2bfloat16_rn(0.f);
+        continue;
+      }
+      const uint32_t buf = vi & 1u;
+      // A failed (timed-out) wait still runs the exchange rounds so the four
+      // warps meet at every bar.sync; nothing is stored from such an item.
+      const bool got = wait(&tfull[buf], (vi >> 1) & 1u);
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + buf * TC_NMAX;
+      for (int c0 = 0; c0 < cnt; c0 += TC_XCH) {
+        // Column of member c = its token; members past cnt re-read column 0.
+        uint32_t v[TC_XCH];
+#pragma unroll
+        for (int j = 0; j < TC_XCH; ++j) {
+          const int tok = c0 + j < cnt ? r.mtok[beg + c0 + j] : 0;
+          v[j] = tmem_ld_x1(taddr + (uint32_t)tok);
+        }
+        tmem_wait_ld();
+        if (!is_gate) {
+#pragma unroll
+          for (int j = 0; j < TC_XCH; ++j) xch[j * TC_NEUR + 32 * (q & 1) + lane] = __uint_as_float(v[j]);
+        }
+        named_barrier_sync(1, 128);
+        if (is_gate && got && nn < I) {
+#pragma unroll
+          for (int j = 0; j < TC_XCH; ++j) {
+            if (c0 + j < cnt) {
+              const float u = xch[j * TC_NEUR + 32 * q + lane];
+              a.out[(size_t)r.members[beg + c0 + j] * I + nn] =
+                  __float2bfloat16_rn(silu_f32(__uint_as_float(v[j])) * u);
+            }
+          }
+        }
+        named_barrier_sync(1, 128);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      ++vi;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_TMEM_COLS);
+  }
+}
+
+}  // namespace wdb

@@ -16,8 +16,11 @@
 #include <mutex>
 #include <string>
 
+#include <atomic>
+
 #include "wd_down.cuh"
 #include "wd_gate_up.cuh"
+#include "wd_gate_up_tc.cuh"
 
 namespace {
 
@@ -57,6 +60,7 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -97,6 +101,118 @@ int check_common(int B, int E, int topk, int hidden, int inter) {
   return WD_OK;
 }
 
+// ---- gate_up path selection -------------------------------------------------
+// 0 = automatic (tensor cores from WD_TC_MIN_TOKENS tokens per launch),
+// 1 = SIMT kernel only, 2 = tensor-core kernel wherever it applies.
+#ifndef WD_TC_MIN_TOKENS
+#define WD_TC_MIN_TOKENS 4
+#endif
+#ifndef WD_TC_KCH
+#define WD_TC_KCH 4
+#endif
+#ifndef WD_TC_L2PROMO
+#define WD_TC_L2PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+std::atomic<int> g_gate_up_path{-1};
+
+int gate_up_path() {
+  int p = g_gate_up_path.load(std::memory_order_relaxed);
+  if (p < 0) {
+    const char* v = std::getenv("WARP_DECODE_GATE_UP");
+    p = 0;
+    if (v && std::strcmp(v, "simt") == 0) p = 1;
+    if (v && std::strcmp(v, "tc") == 0) p = 2;
+    int expected = -1;
+    g_gate_up_path.compare_exchange_strong(expected, p);
+    p = g_gate_up_path.load(std::memory_order_relaxed);
+  }
+  return p;
+}
+
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Tensor-core gate_up for one launch chunk of bn tokens.
+int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const int32_t* ids,
+                      void* out, int bn, int E, int topk, int hidden, int inter,
+                      uint32_t* status, cudaStream_t s) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap tm_w, tm_x;
+  // w_gate_up [E, 2I, H] viewed as (k, neuron, gate|up, expert): one box is
+  // 64 K-columns of 64 gate rows followed by the 64 matching up rows.
+  const cuuint64_t wdim[4] = {(cuuint64_t)hidden, (cuuint64_t)inter, 2, (cuuint64_t)E};
+  const cuuint64_t wstr[3] = {(cuuint64_t)hidden * 2, (cuuint64_t)inter * hidden * 2,
+                              (cuuint64_t)2 * inter * hidden * 2};
+  const cuuint32_t wbox[4] = {(cuuint32_t)wdb::TC_BK, (cuuint32_t)wdb::TC_NEUR, 2, 1};
+  const cuuint32_t ones[4] = {1, 1, 1, 1};
+  CUresult cr = enc(&tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(w), wdim, wstr,
+                    wbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    WD_TC_L2PROMO, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_gate_up) encode failed");
+  const cuuint64_t xdim[2] = {(cuuint64_t)hidden, (cuuint64_t)bn};
+  const cuuint64_t xstr[1] = {(cuuint64_t)hidden * 2};
+  const int npad = (bn + 15) / 16 * 16;  // MMA N; rows past bn are zero-filled
+  const cuuint32_t xbox[2] = {(cuuint32_t)wdb::TC_BK, (cuuint32_t)npad};
+  cr = enc(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdim, xstr, xbox,
+           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (x) encode failed");
+
+  const int n = bn * topk;
+  const int budget = dev->smem_optin - 2048;
+  // Stages of WD_TC_KCH 64-wide K chunks (each weight row is then read in
+  // WD_TC_KCH * 128 contiguous bytes), as many as fit, at most 8.
+  const int kch = WD_TC_KCH;
+  int stages = 8;
+  while (stages > 2 && wdb::gate_up_tc_smem_bytes(stages, kch, npad, n, E) > budget) --stages;
+  const int smem = wdb::gate_up_tc_smem_bytes(stages, kch, npad, n, E);
+  if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+  wdb::GateUpTcArgs a;
+  a.ids = ids;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.status = status;
+  a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+  a.stages = stages;
+  a.npad = npad;
+  a.kch = kch;
+  const long long work = (long long)n * ((inter + wdb::TC_NEUR - 1) / wdb::TC_NEUR);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+  cfg.blockDim = dim3(wdb::TC_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = s;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_kernel, tm_w, tm_x, a);
+  if (err != cudaSuccess)
+    return fail(WD_ERR_CUDA, std::string("gate_up (tensor core) launch: ") + cudaGetErrorString(err));
+  return WD_OK;
+}
+
+// Whether a call of B tokens runs on the tensor-core kernel (in launches of
+// at most TC_NMAX tokens).
+bool gate_up_tc_applies(int B, int E, int hidden) {
+  const int p = gate_up_path();
+  if (p == 1) return false;
+  if (E > wdb::MAX_DEDUP_E || hidden % 8 != 0) return false;
+  return p == 2 || B >= WD_TC_MIN_TOKENS;
+}
+
 template <int FMT>
 int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const int32_t* ids,
                  void* out, int B, int E, int topk, int hidden, int inter, uint32_t* status,
@@ -118,13 +234,23 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   if ((rc = device_info(&dev))) return rc;
 
   constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
-  const int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
+  const bool tc = FMT == wdb::W_BF16 && gate_up_tc_applies(B, E, hidden);
+  int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
+  if (tc) tb = std::min(tb, wdb::TC_NMAX);
   if ((long long)std::min(tb, B) * topk * inter >= (1LL << 31))
     return fail(WD_ERR_UNSUPPORTED, "B*topk*inter per launch must be < 2^31");
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
+    if (tc) {
+      rc = gate_up_tc_launch(dev, reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden,
+                             w, ids + (size_t)b0 * topk,
+                             reinterpret_cast<__nv_bfloat16*>(out) + (size_t)b0 * topk * inter, bn,
+                             E, topk, hidden, inter, status, s);
+      if (rc) return rc;
+      continue;
+    }
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
     // Ring: 8 warps x `depth` slots of (gate, up) row chunks of 4 KB each; x
     // staged in shared memory if it fits in 128 KB.  Preference order: a
@@ -316,6 +442,13 @@ int wd_moe_down_3d_batched_mxfp8(const void* h, const uint8_t* w_q, const uint8_
   g_last_error.clear();
   return down_impl<wdb::W_E4M3>(h, w_q, w_scale, topk_ids, topk_scale, y_out, out_fp32, B, E,
                                 topk, hidden, inter, status, stream);
+}
+
+int wd_set_gate_up_path(int path) {
+  g_last_error.clear();
+  if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
+  g_gate_up_path.store(path);
+  return WD_OK;
 }
 
 int wd_status_read(uint32_t* value, int clear) {
