@@ -138,13 +138,22 @@ WD_API int wd_status_read(uint32_t* value, int clear);
 /*
  * Choose the kernel behind wd_moe_gate_up_3d_batched (bf16 weights), for all
  * later calls in this process: 0 = automatic (tcgen05 tensor-core kernel from
- * 4 tokens per launch, SIMT kernel below), 1 = SIMT kernel only, 2 = tensor-
+ * 16 tokens per call, SIMT kernel below), 1 = SIMT kernel only, 2 = tensor-
  * core kernel wherever it applies (E <= 1024).  Both give
  * the same result within bf16 rounding of the FP32 sums.  The environment
  * variable WARP_DECODE_GATE_UP=simt|tc sets the initial choice.  No
  * counterpart in the reference (it has one kernel per op).
  */
 WD_API int wd_set_gate_up_path(int path);
+
+/*
+ * The same choice for wd_moe_down_3d_batched (bf16 weights): 0 = automatic
+ * (tcgen05 kernel from 32 tokens per call), 1 = SIMT kernel only, 2 = tensor-
+ * core kernel wherever it applies (inter <= 256, E <= 1024, hidden <= 64 x
+ * the SM count).  WARP_DECODE_DOWN=simt|tc sets the initial choice.  No
+ * counterpart in the reference.
+ */
+WD_API int wd_set_down_path(int path);
 
 #ifdef __cplusplus
 }  /* extern "C" */

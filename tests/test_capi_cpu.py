@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 9, names
+    assert len(names) == 10, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -31,6 +31,9 @@ def test_gate_up_path_selector_validates():
     assert b"path" in L.wd_last_error_message()
     for p in (capi.GATE_UP_SIMT, capi.GATE_UP_TC, capi.GATE_UP_AUTO):
         assert L.wd_set_gate_up_path(p) == capi.WD_OK
+    assert L.wd_set_down_path(-1) == capi.WD_ERR_SHAPE
+    for p in (capi.PATH_SIMT, capi.PATH_TC, capi.PATH_AUTO):
+        assert L.wd_set_down_path(p) == capi.WD_OK
 
 
 def test_version_and_error_strings():

@@ -37,10 +37,12 @@ _SIGS = {
     "wd_moe_down_3d_batched_mxfp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "wd_status_read": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
     "wd_set_gate_up_path": (_I, [_I]),
+    "wd_set_down_path": (_I, [_I]),
 }
 
-# Values of wd_set_gate_up_path.
+# Values of wd_set_gate_up_path / wd_set_down_path.
 GATE_UP_AUTO, GATE_UP_SIMT, GATE_UP_TC = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TC = 0, 1, 2
 
 _lib = None
 
@@ -101,6 +103,11 @@ def down_mxfp8(h, wq, ws, ids, scale, out, out_fp32, B, E, topk, hidden, inter, 
 def set_gate_up_path(path: int) -> None:
     """Select the gate_up kernel for later calls (GATE_UP_AUTO / _SIMT / _TC)."""
     check(lib().wd_set_gate_up_path(int(path)))
+
+
+def set_down_path(path: int) -> None:
+    """Select the down kernel for later calls (PATH_AUTO / PATH_SIMT / PATH_TC)."""
+    check(lib().wd_set_down_path(int(path)))
 
 
 def status_read(clear: bool = True) -> int:

@@ -180,6 +180,7 @@ int64_t status(bool clear, int64_t device) {
 }
 
 void set_gate_up_path(int64_t path) { check_rc(wd_set_gate_up_path(static_cast<int>(path))); }
+void set_down_path(int64_t path) { check_rc(wd_set_down_path(static_cast<int>(path))); }
 
 }  // namespace
 
@@ -205,5 +206,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("clear") = true, py::arg("device") = 0);
   m.def("set_gate_up_path", &set_gate_up_path,
         "gate_up kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
+        py::arg("path"));
+  m.def("set_down_path", &set_down_path,
+        "down kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
         py::arg("path"));
 }

@@ -214,22 +214,22 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
 // pipeline uniform) and give it a zero result.
 struct RouteSmem {
   int* ids;      // [n]   expert of each slot (validated, -1 if invalid)
-  int* tab;      // [E]   dedup table: min slot index, then group rank
-  int* aux;      // [n]   scratch
-  int* rank;     // [n]   group rank of each slot
-  int* gcnt;     // [n]   members per group
-  int* goff;     // [n]   first member index of each group
-  int* members;  // [n]   slots ordered by (group, slot)
+  int* rank;     // [n]   position of each slot among its expert's slots
+  int* aux;      // [n]   free for the kernels (per-group scratch)
+  int* members;  // [n]   slots ordered by (expert, slot); invalid slots last
   int* mtok;     // [n]   token (slot / topk) of each entry of `members`
-  int* sg_exp;   // [n]   expert of each capped group (-1: invalid slot)
+  int* sg_exp;   // [n]   expert of each capped group (-1: invalid ids)
   int* sg_beg;   // [n]   first member (index into members) of each capped group
   int* sg_cnt;   // [n]   member count of each capped group
   int* nsg;      // [1]   number of capped groups
+  int* cnt;      // [E+1] slots per expert (entry E: invalid ids)     (dedup only)
+  int* off;      // [E+1] first member index of each expert           (dedup only)
+  int* wsum;     // [64]  per-warp partial sums of the scan           (dedup only)
 };
 
 // Shared-memory bytes needed by RouteSmem for n slots and E experts.
 __host__ __device__ inline int route_smem_bytes(int n, int E, bool dedup) {
-  int ints = 11 * n + 1 + (dedup ? E : 0);
+  int ints = 8 * n + 1 + (dedup ? 2 * (E + 1) + 64 : 0);
   return ((ints * 4 + 127) / 128) * 128;
 }
 
@@ -237,59 +237,65 @@ __device__ inline RouteSmem route_carve(int* base, int n, int E, bool dedup) {
   RouteSmem r;
   int* p = base;
   r.ids = p; p += n;
-  r.aux = p; p += n;
   r.rank = p; p += n;
-  r.gcnt = p; p += n;
-  r.goff = p; p += n;
+  r.aux = p; p += n;
   r.members = p; p += n;
   r.mtok = p; p += n;
   r.sg_exp = p; p += n;
   r.sg_beg = p; p += n;
   r.sg_cnt = p; p += n;
   r.nsg = p; p += 1;
-  r.tab = dedup ? p : nullptr;
+  r.cnt = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
+  r.off = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
+  r.wsum = dedup ? p : nullptr;
   return r;
 }
 
-// Exclusive prefix sum of a[0..cnt) in place by one warp (lanes in step);
-// returns the total.  cnt <= MAX_SLOTS.
-__device__ __forceinline__ int warp_exclusive_scan(int* a, int cnt, int lane) {
-  int base = 0;
-  for (int c = 0; c < cnt; c += 32) {
-    const int i = c + lane;
-    const int v = i < cnt ? a[i] : 0;
-    int inc = v;
+struct NoInit {
+  __device__ void operator()() const {}
+};
+
+// Routing of one launch, computed by every CTA (all threads; ends with
+// __syncthreads).  Validates topk_ids (out-of-range ids become -1 and raise
+// WD_STATUS_BAD_EXPERT_ID), then groups the slots by expert:
+//  * dedup: one group per touched expert, in ascending expert id, members
+//    in slot order, split into groups of at most `cap` members; all invalid
+//    slots form the last group(s) with expert -1.  A stable counting sort:
+//    one warp ranks the slots 32 at a time (match_any), one block-wide scan
+//    places the experts.  Same result in every CTA: deterministic.
+//  * no dedup: every slot is its own group (slot order).
+// `init` runs after the id loads are issued and before they are used, so a
+// caller's own set-up (barrier init) overlaps the global-memory latency.
+// The grouping follows the outputs-not-experts idea of the reference (no
+// align/permute pass over unsorted topk_ids, csrc/moe_gate_up_3d_batched.cu)
+// but shares each expert's weight stream between the slots routed to it.
+template <class Init = NoInit>
+__device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict__ topk_ids,
+                                   int n, int E, int K, bool dedup, int cap, uint32_t* status,
+                                   Init init = Init()) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  constexpr int PER = (MAX_SLOTS + 127) / 128;  // ids per thread (blockDim >= 128)
+  int ev[PER];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += t;
-    }
-    if (i < cnt) a[i] = base + inc - v;
-    base += __shfl_sync(0xffffffffu, inc, 31);
+  for (int k = 0; k < PER; ++k) {
+    const int i = tid + k * nt;
+    ev[k] = i < n ? __ldg(topk_ids + i) : 0;
   }
-  return base;
-}
-
-// Load and validate this launch's topk_ids into shared memory.  All threads.
-// Ends with __syncthreads().
-__device__ inline void load_ids(const RouteSmem& r, const int32_t* __restrict__ topk_ids, int n,
-                                int E, uint32_t* status) {
+  init();
+  if (dedup)
+    for (int e = tid; e <= E; e += nt) r.cnt[e] = 0;
   bool bad = false;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    int e = __ldg(topk_ids + i);
-    if (e < 0 || e >= E) { e = -1; bad = true; }
-    r.ids[i] = e;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = tid + k * nt;
+    if (i < n) {
+      int e = ev[k];
+      if (e < 0 || e >= E) { e = -1; bad = true; }
+      r.ids[i] = e;
+    }
   }
-  if (__syncthreads_or(bad) && threadIdx.x == 0) raise_status(status, WD_STATUS_BAD_EXPERT_ID);
-}
-
-// Build the capped groups from r.ids (see load_ids).  All threads; ends with
-// __syncthreads().
-__device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, bool dedup,
-                                    int cap = GROUP_MAX) {
-  const int tid = threadIdx.x;
-  const int nt = blockDim.x;
-  const int lane = tid & 31;
+  if (__syncthreads_or(bad) && tid == 0) raise_status(status, WD_STATUS_BAD_EXPERT_ID);
   if (!dedup) {
     for (int i = tid; i < n; i += nt) {
       r.sg_exp[i] = r.ids[i];
@@ -302,80 +308,64 @@ __device__ inline void build_groups(const RouteSmem& r, int n, int E, int K, boo
     __syncthreads();
     return;
   }
-  __shared__ int s_groups;
-  for (int e = tid; e < E; e += nt) r.tab[e] = 0x7fffffff;
-  for (int i = tid; i < n; i += nt) r.gcnt[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += nt) {
-    const int e = r.ids[i];
-    if (e >= 0) atomicMin(&r.tab[e], i);
-  }
-  __syncthreads();
-  // A group opens at the first slot of each expert and at every invalid slot.
-  for (int i = tid; i < n; i += nt) {
-    const int e = r.ids[i];
-    const int open = (e < 0 || r.tab[e] == i) ? 1 : 0;
-    r.aux[i] = open;
-    r.rank[i] = open;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    const int groups = warp_exclusive_scan(r.rank, n, lane);  // rank of opening slots
-    if (lane == 0) s_groups = groups;
-  }
-  __syncthreads();
-  for (int i = tid; i < n; i += nt) {
-    if (r.aux[i]) {
-      const int e = r.ids[i];
-      if (e >= 0) r.tab[e] = r.rank[i];
+  // Stable rank within each expert (bucket E collects invalid slots).
+  if (warp == 0) {
+    for (int c = 0; c < n; c += 32) {
+      const int i = c + lane;
+      const bool v = i < n;
+      const int key = v ? (r.ids[i] < 0 ? E : r.ids[i]) : E + 1 + lane;
+      const unsigned m = __match_any_sync(0xffffffffu, key);
+      const int base = v ? r.cnt[key] : 0;
+      __syncwarp();
+      if (v) {
+        r.rank[i] = base + __popc(m & ((1u << lane) - 1u));
+        if (lane == __ffs(m) - 1) r.cnt[key] = base + __popc(m);
+      }
+      __syncwarp();
     }
   }
   __syncthreads();
-  // Every slot learns its group; counts and (unordered) positions by atomics.
-  for (int i = tid; i < n; i += nt) {
-    const int e = r.ids[i];
-    const int g = (e < 0) ? r.rank[i] : r.tab[e];
-    r.rank[i] = g;
-    r.aux[i] = atomicAdd(&r.gcnt[g], 1);
+  // Exclusive scans over the E + 1 buckets: member offsets and capped-group
+  // indices, each thread owning a contiguous run of buckets.
+  const int NE = E + 1;
+  const int per = (NE + nt - 1) / nt;
+  const int e0 = min(NE, tid * per), e1 = min(NE, e0 + per);
+  int sc = 0, ss = 0;
+  for (int e = e0; e < e1; ++e) {
+    const int c = r.cnt[e];
+    sc += c;
+    ss += (c + cap - 1) / cap;
   }
-  __syncthreads();
-  const int groups = s_groups;
-  if (tid < 32) {
-    for (int g = lane; g < groups; g += 32) r.goff[g] = r.gcnt[g];
-    __syncwarp();
-    warp_exclusive_scan(r.goff, groups, lane);
+  int ic = sc, is = ss;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t1 = __shfl_up_sync(0xffffffffu, ic, o);
+    const int t2 = __shfl_up_sync(0xffffffffu, is, o);
+    if (lane >= o) { ic += t1; is += t2; }
   }
+  if (lane == 31) { r.wsum[2 * warp] = ic; r.wsum[2 * warp + 1] = is; }
   __syncthreads();
-  for (int i = tid; i < n; i += nt) r.members[r.goff[r.rank[i]] + r.aux[i]] = i;
-  __syncthreads();
-  // Members in slot order (groups are small: insertion sort per group), and
-  // the number of capped groups per group.
-  for (int g = tid; g < groups; g += nt) {
-    const int b = r.goff[g], c = r.gcnt[g];
-    for (int x = b + 1; x < b + c; ++x) {
-      const int v = r.members[x];
-      int y = x - 1;
-      while (y >= b && r.members[y] > v) { r.members[y + 1] = r.members[y]; --y; }
-      r.members[y + 1] = v;
-    }
-    r.aux[g] = (c + cap - 1) / cap;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    const int total = warp_exclusive_scan(r.aux, groups, lane);
-    if (lane == 0) *r.nsg = total;
-  }
-  __syncthreads();
-  for (int g = tid; g < groups; g += nt) {
-    const int b = r.goff[g], c = r.gcnt[g], s0 = r.aux[g];
-    const int e = r.ids[r.members[b]];
+  int oc = ic - sc, os = is - ss;
+  for (int w = 0; w < warp; ++w) { oc += r.wsum[2 * w]; os += r.wsum[2 * w + 1]; }
+  for (int e = e0; e < e1; ++e) {
+    const int c = r.cnt[e];
+    r.off[e] = oc;
     for (int j = 0; j * cap < c; ++j) {
-      r.sg_exp[s0 + j] = e;
-      r.sg_beg[s0 + j] = b + j * cap;
-      r.sg_cnt[s0 + j] = min(cap, c - j * cap);
+      r.sg_exp[os] = e < E ? e : -1;
+      r.sg_beg[os] = oc + j * cap;
+      r.sg_cnt[os] = min(cap, c - j * cap);
+      ++os;
     }
+    oc += c;
   }
-  for (int i = tid; i < n; i += nt) r.mtok[i] = r.members[i] / K;
+  if (tid == nt - 1) *r.nsg = os;
+  __syncthreads();
+  for (int i = tid; i < n; i += nt) {
+    const int e = r.ids[i];
+    const int p = r.off[e < 0 ? E : e] + r.rank[i];
+    r.members[p] = i;
+    r.mtok[p] = i / K;
+  }
   __syncthreads();
 }
 

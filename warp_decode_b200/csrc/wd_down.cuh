@@ -227,8 +227,7 @@ __global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < NCW * tile; i += blockDim.x) tiles[i] = 0.f;
-  load_ids(r, a.ids, n, a.E, a.status);  // before the wait: may be re-checked
-  build_groups(r, n, a.E, a.K, dedup);
+  route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);  // before the wait: re-checked
 
   auto warp_total = [&](int w) {
     const int items = *r.nsg * cpg;
@@ -291,8 +290,7 @@ __global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
     // The preceding kernel rewrote topk_ids after signalling early: rebuild
     // from the settled ids; prefetched stages are drained, not used.
     if (threadIdx.x == 0) raise_status(a.status, WD_STATUS_ROUTING_CHANGED);
-    load_ids(r, a.ids, n, a.E, a.status);
-    build_groups(r, n, a.E, a.K, dedup);
+    route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);
     if (warp < NCW) pos0 = ctrl[24 + warp];
   }
 

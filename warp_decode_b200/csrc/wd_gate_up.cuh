@@ -204,8 +204,7 @@ __global__ void __maxnreg__(112) moe_gate_up_kernel(const GateUpArgs a) {
       bulk_g2s_big(xs, a.x, x_bytes, xbar, l2_policy_evict_last());
     }
   }
-  load_ids(r, a.ids, n, a.E, a.status);   // ends with __syncthreads
-  build_groups(r, n, a.E, a.K, dedup);    // ends with __syncthreads
+  route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);  // ends with __syncthreads
 
   const int nsg = *r.nsg;
   const int items = nsg * a.I;  // host guarantees n * I < 2^31

@@ -90,28 +90,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+  // Barrier set-up and the TMEM allocation overlap the topk_ids loads.
+  auto setup = [&]() {
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < S; ++s) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], 1);
+      }
+      mbar_init(&tfull[0], 1);
+      mbar_init(&tfull[1], 1);
+      mbar_init(&tempty[0], 4);
+      mbar_init(&tempty[1], 4);
+      mbar_init(done, 1);
+      ctrl[0] = 0;
+      fence_mbar_init();
     }
-    mbar_init(&tfull[0], 1);
-    mbar_init(&tfull[1], 1);
-    mbar_init(&tempty[0], 4);
-    mbar_init(&tempty[1], 4);
-    mbar_init(done, 1);
-    ctrl[0] = 0;
-    fence_mbar_init();
-    prefetch_tensormap(&tm_w);
-    prefetch_tensormap(&tm_x);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, TC_TMEM_COLS);
-    tmem_relinquish();
-    tc_fence_before();
-  }
-  load_ids(r, a.ids, n, a.E, a.status);           // ends with __syncthreads
-  build_groups(r, n, a.E, a.K, true, MAX_SLOTS);  // ends with __syncthreads
+    if (threadIdx.x == 32) {
+      prefetch_tensormap(&tm_w);
+      prefetch_tensormap(&tm_x);
+    }
+    if (warp == 1) {
+      tmem_alloc(tmem_slot, TC_TMEM_COLS);
+      tmem_relinquish();
+      tc_fence_before();
+    }
+  };
+  route_build(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status, setup);  // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -248,6 +252,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // A failed (timed-out) wait still runs the exchange rounds so the four
       // warps meet at every bar.sync; nothing is stored from such an item.
       const bool got = wait(&tfull[buf], (vi >> 1) & 1u);
+      __syncwarp();  // tcgen05.ld and bar.sync below are warp-collective
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + buf * TC_NMAX;
       for (int c0 = 0; c0 < cnt; c0 += TC_XCH) {

@@ -21,6 +21,7 @@
 #include "wd_down.cuh"
 #include "wd_gate_up.cuh"
 #include "wd_gate_up_tc.cuh"
+#include "wd_down_tc.cuh"
 
 namespace {
 
@@ -61,6 +62,9 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<16>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<32>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<64>),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -105,7 +109,10 @@ int check_common(int B, int E, int topk, int hidden, int inter) {
 // 0 = automatic (tensor cores from WD_TC_MIN_TOKENS tokens per launch),
 // 1 = SIMT kernel only, 2 = tensor-core kernel wherever it applies.
 #ifndef WD_TC_MIN_TOKENS
-#define WD_TC_MIN_TOKENS 4
+#define WD_TC_MIN_TOKENS 16
+#endif
+#ifndef WD_DTC_MIN_TOKENS
+#define WD_DTC_MIN_TOKENS 32
 #endif
 #ifndef WD_TC_KCH
 #define WD_TC_KCH 4
@@ -114,20 +121,25 @@ int check_common(int B, int E, int topk, int hidden, int inter) {
 #define WD_TC_L2PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
 #endif
 std::atomic<int> g_gate_up_path{-1};
+std::atomic<int> g_down_path{-1};
 
-int gate_up_path() {
-  int p = g_gate_up_path.load(std::memory_order_relaxed);
+// Current choice of one kernel's path; the first call reads the environment.
+int kernel_path(std::atomic<int>& slot, const char* env) {
+  int p = slot.load(std::memory_order_relaxed);
   if (p < 0) {
-    const char* v = std::getenv("WARP_DECODE_GATE_UP");
+    const char* v = std::getenv(env);
     p = 0;
     if (v && std::strcmp(v, "simt") == 0) p = 1;
     if (v && std::strcmp(v, "tc") == 0) p = 2;
     int expected = -1;
-    g_gate_up_path.compare_exchange_strong(expected, p);
-    p = g_gate_up_path.load(std::memory_order_relaxed);
+    slot.compare_exchange_strong(expected, p);
+    p = slot.load(std::memory_order_relaxed);
   }
   return p;
 }
+
+int gate_up_path() { return kernel_path(g_gate_up_path, "WARP_DECODE_GATE_UP"); }
+int down_path() { return kernel_path(g_down_path, "WARP_DECODE_DOWN"); }
 
 // cuTensorMapEncodeTiled from the driver, resolved once through the runtime.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -302,6 +314,74 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   return WD_OK;
 }
 
+// Rows per CTA of the tensor-core down kernel (its MMA N): the smallest of
+// 16 / 32 / 64 that covers hidden with at most one CTA per SM; 0 if none.
+int down_tc_rows(int hidden, int sms) {
+  for (int R : {16, 32, 64})
+    if ((hidden + R - 1) / R <= sms) return R;
+  return 0;
+}
+
+bool down_tc_applies(int B, int E, int hidden, int inter, int sms) {
+  const int p = down_path();
+  if (p == 1) return false;
+  if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK) return false;
+  if (down_tc_rows(hidden, sms) == 0) return false;
+  return p == 2 || B >= WD_DTC_MIN_TOKENS;
+}
+
+// Tensor-core down for one launch chunk of bn tokens.
+int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const int32_t* ids,
+                   const float* scale, void* out, int out_fp32, int bn, int E, int topk,
+                   int hidden, int inter, uint32_t* status, cudaStream_t s) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int R = down_tc_rows(hidden, dev->sm_count);
+  // w_down [E, H, I]: box = 64 K-columns of R rows of one expert.
+  CUtensorMap tm;
+  const cuuint64_t dim[3] = {(cuuint64_t)inter, (cuuint64_t)hidden, (cuuint64_t)E};
+  const cuuint64_t str[2] = {(cuuint64_t)inter * 2, (cuuint64_t)hidden * inter * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)wdb::DTC_BK, (cuuint32_t)R, 1};
+  const cuuint32_t ones[3] = {1, 1, 1};
+  CUresult cr = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dim, str, box,
+                    ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_down) encode failed");
+  const int n = bn * topk;
+  const int budget = dev->smem_optin - 2048;
+  int stages = 12;
+  while (stages > 2 && wdb::down_tc_smem_bytes(stages, R, inter, bn, n, E) > budget) --stages;
+  const int smem = wdb::down_tc_smem_bytes(stages, R, inter, bn, n, E);
+  if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+  wdb::DownTcArgs a;
+  a.h = reinterpret_cast<const __nv_bfloat16*>(h);
+  a.ids = ids;
+  a.scale = scale;
+  a.out = out;
+  a.out_fp32 = out_fp32 ? 1 : 0;
+  a.status = status;
+  a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+  a.R = R;
+  a.stages = stages;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((hidden + R - 1) / R));
+  cfg.blockDim = dim3(wdb::DTC_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t err;
+  if (R == 16) err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<16>, tm, a);
+  else if (R == 32) err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<32>, tm, a);
+  else err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<64>, tm, a);
+  if (err != cudaSuccess)
+    return fail(WD_ERR_CUDA, std::string("down (tensor core) launch: ") + cudaGetErrorString(err));
+  return WD_OK;
+}
+
 template <int FMT>
 int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int32_t* ids,
               const float* scale, void* out, int out_fp32, int B, int E, int topk, int hidden,
@@ -340,6 +420,8 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
   // Tokens per launch: routing capacity and the 8 per-warp FP32 tiles.
   int tb = std::max(1, wdb::MAX_SLOTS / topk);
   tb = std::min(tb, std::max(1, (64 * 1024) / (4 * wdb::NWARPS * rows_max)));
+  const bool tc = FMT == wdb::W_BF16 && down_tc_applies(B, E, hidden, inter, dev->sm_count);
+  if (tc) tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), 64);
 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -349,6 +431,14 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
   for (int b0 = 0; b0 < B; b0 += tb) {
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
+    if (tc) {
+      rc = down_tc_launch(dev, reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter,
+                          w, ids + (size_t)b0 * topk, scale + (size_t)b0 * topk,
+                          reinterpret_cast<uint8_t*>(out) + (size_t)b0 * hidden * out_elem,
+                          out_fp32, bn, E, topk, hidden, inter, status, s);
+      if (rc) return rc;
+      continue;
+    }
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
     const long long h_bytes = (long long)n * inter * 2;
     bool h_smem = h_bytes <= 64 * 1024;
@@ -448,6 +538,13 @@ int wd_set_gate_up_path(int path) {
   g_last_error.clear();
   if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
   g_gate_up_path.store(path);
+  return WD_OK;
+}
+
+int wd_set_down_path(int path) {
+  g_last_error.clear();
+  if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
+  g_down_path.store(path);
   return WD_OK;
 }
 
