@@ -148,8 +148,8 @@ WD_API int wd_set_gate_up_path(int path);
 
 /*
  * The same choice for wd_moe_down_3d_batched (bf16 weights): 0 = automatic
- * (tcgen05 kernel from 32 tokens per call), 1 = SIMT kernel only, 2 = tensor-
- * core kernel wherever it applies (inter <= 256, E <= 1024, hidden <= 64 x
+ * (tcgen05 kernel from 2 tokens per call), 1 = SIMT kernel only, 2 = tensor-
+ * core kernel wherever it applies (inter <= 256, E <= 1024, hidden <= 128 x
  * the SM count).  WARP_DECODE_DOWN=simt|tc sets the initial choice.  No
  * counterpart in the reference.
  */

@@ -84,14 +84,14 @@ def test_qwen3_tp8_both_paths(wd, B):
 
 
 @pytest.mark.parametrize("B,E,K,H,I,routing", [
-    (3, 5, 3, 264, 40, "randint"),      # inter % 64 != 0 (zero K tail), hidden % 16 != 0
+    (3, 5, 3, 264, 40, "randint"),      # inter % 64 != 0 (zero K tail), hidden % 128 != 0
     (2, 1, 4, 128, 8, "randint"),       # one expert, inter = 8
-    (64, 2, 8, 256, 32, "randint"),     # ~256 slots per expert: groups split at 128
-    (5, 6, 6, 128, 64, "randint"),      # repeated ids inside a token (ordered rounds)
+    (64, 2, 8, 256, 32, "randint"),     # ~256 slots per expert: items of 16 members
+    (5, 6, 6, 128, 64, "randint"),      # repeated ids inside a token (fixed add order)
     (100, 64, 8, 512, 64, "uniform"),   # B*topk > 512: two launches
     (4, 2048, 8, 256, 64, "uniform"),   # E > 1024: SIMT path
     (2, 16, 4, 512, 1544, "uniform"),   # inter > 256: SIMT path
-    (8, 256, 8, 7168, 256, "zipf"),     # DeepSeek-V3 TP=8 shard: 64 rows per CTA
+    (8, 256, 8, 7168, 256, "zipf"),     # DeepSeek-V3 TP=8 shard: 56 tiles, clusters of 2
     (16, 128, 8, 2048, 768, "uniform"), # Qwen3-30B shape, bf16 (SIMT: inter > 256)
 ])
 def test_shapes_tc(wd, B, E, K, H, I, routing):

@@ -16,7 +16,9 @@
 #include <mutex>
 #include <string>
 
+#include <array>
 #include <atomic>
+#include <vector>
 
 #include "wd_down.cuh"
 #include "wd_gate_up.cuh"
@@ -62,9 +64,7 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel),
-        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<16>),
-        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<32>),
-        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<64>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -112,7 +112,7 @@ int check_common(int B, int E, int topk, int hidden, int inter) {
 #define WD_TC_MIN_TOKENS 16
 #endif
 #ifndef WD_DTC_MIN_TOKENS
-#define WD_DTC_MIN_TOKENS 32
+#define WD_DTC_MIN_TOKENS 2
 #endif
 #ifndef WD_TC_KCH
 #define WD_TC_KCH 4
@@ -314,34 +314,68 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   return WD_OK;
 }
 
-// Rows per CTA of the tensor-core down kernel (its MMA N): the smallest of
-// 16 / 32 / 64 that covers hidden with at most one CTA per SM; 0 if none.
-int down_tc_rows(int hidden, int sms) {
-  for (int R : {16, 32, 64})
-    if ((hidden + R - 1) / R <= sms) return R;
-  return 0;
+// Largest cluster size CL in {8, 4, 2, 1} such that the ceil(hidden / 128)
+// row tiles times CL CTAs fit on the SMs at once (checked with the
+// occupancy calculator for this launch configuration); 0 if none.
+int down_tc_cluster(const DeviceInfo* dev, int hidden, int smem) {
+  static std::mutex mu;
+  static std::vector<std::array<int, 4>> cache;  // {device, hidden, smem, CL}
+  int devno = 0;
+  cudaGetDevice(&devno);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& c : cache)
+      if (c[0] == devno && c[1] == hidden && c[2] == smem) return c[3];
+  }
+  const int T = (hidden + wdb::DTC_M - 1) / wdb::DTC_M;
+  int best = 0;
+  for (int cl : {8, 4, 2, 1}) {
+    if (T * cl > dev->sm_count) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(T * cl));
+    cfg.blockDim = dim3(wdb::DTC_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_down_tc_kernel, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (nc >= T) { best = cl; break; }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({devno, hidden, smem, best});
+  return best;
 }
 
 bool down_tc_applies(int B, int E, int hidden, int inter, int sms) {
   const int p = down_path();
   if (p == 1) return false;
   if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK) return false;
-  if (down_tc_rows(hidden, sms) == 0) return false;
+  if ((hidden + wdb::DTC_M - 1) / wdb::DTC_M > sms) return false;
   return p == 2 || B >= WD_DTC_MIN_TOKENS;
 }
 
-// Tensor-core down for one launch chunk of bn tokens.
+// Tensor-core down for one launch chunk of bn tokens; returns WD_ERR_UNSUPPORTED
+// (nothing launched) if no cluster configuration fits, so the caller can
+// fall back to the SIMT kernel.
 int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const int32_t* ids,
                    const float* scale, void* out, int out_fp32, int bn, int E, int topk,
                    int hidden, int inter, uint32_t* status, cudaStream_t s) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  const int R = down_tc_rows(hidden, dev->sm_count);
-  // w_down [E, H, I]: box = 64 K-columns of R rows of one expert.
+  // w_down [E, H, I]: box = 64 K-columns of 128 rows of one expert.
   CUtensorMap tm;
   const cuuint64_t dim[3] = {(cuuint64_t)inter, (cuuint64_t)hidden, (cuuint64_t)E};
   const cuuint64_t str[2] = {(cuuint64_t)inter * 2, (cuuint64_t)hidden * inter * 2};
-  const cuuint32_t box[3] = {(cuuint32_t)wdb::DTC_BK, (cuuint32_t)R, 1};
+  const cuuint32_t box[3] = {(cuuint32_t)wdb::DTC_BK, (cuuint32_t)wdb::DTC_M, 1};
   const cuuint32_t ones[3] = {1, 1, 1};
   CUresult cr = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dim, str, box,
                     ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -349,10 +383,14 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_down) encode failed");
   const int n = bn * topk;
   const int budget = dev->smem_optin - 2048;
-  int stages = 12;
-  while (stages > 2 && wdb::down_tc_smem_bytes(stages, R, inter, bn, n, E) > budget) --stages;
-  const int smem = wdb::down_tc_smem_bytes(stages, R, inter, bn, n, E);
-  if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+  int stages = 4, nbuf = 8;
+  auto need = [&]() { return wdb::down_tc_smem_bytes(stages, nbuf, inter, bn, n, E); };
+  while (need() > budget && nbuf > wdb::DTC_GW) nbuf -= 2;
+  while (need() > budget && stages > 2) --stages;
+  if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+  const int smem = need();
+  const int cl = down_tc_cluster(dev, hidden, smem);
+  if (cl == 0) return fail(WD_ERR_UNSUPPORTED, "no cluster configuration fits");
   wdb::DownTcArgs a;
   a.h = reinterpret_cast<const __nv_bfloat16*>(h);
   a.ids = ids;
@@ -361,22 +399,31 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   a.out_fp32 = out_fp32 ? 1 : 0;
   a.status = status;
   a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
-  a.R = R;
   a.stages = stages;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  a.nbuf = nbuf;
+  a.cl = cl;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cl > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)cl;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((hidden + R - 1) / R));
+  cfg.gridDim = dim3((unsigned)(((hidden + wdb::DTC_M - 1) / wdb::DTC_M) * cl));
   cfg.blockDim = dim3(wdb::DTC_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  cudaError_t err;
-  if (R == 16) err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<16>, tm, a);
-  else if (R == 32) err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<32>, tm, a);
-  else err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<64>, tm, a);
+  cfg.numAttrs = na;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel, tm, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("down (tensor core) launch: ") + cudaGetErrorString(err));
   return WD_OK;
