@@ -213,6 +213,10 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
 // expert -1: kernels stream a valid expert's rows for it (keeping the
 // pipeline uniform) and give it a zero result.
 struct RouteSmem {
+  unsigned long long* mask;  // [E+1] tokens routed to each expert (fast path)  (dedup only)
+  int* cnt;      // [E+1] slots per expert (entry E: invalid ids)           (dedup only)
+  int* off;      // [E+1] first member index of each expert                 (dedup only)
+  int* wsum;     // [64]  per-warp partial sums of the scan                 (dedup only)
   int* ids;      // [n]   expert of each slot (validated, -1 if invalid)
   int* rank;     // [n]   position of each slot among its expert's slots
   int* aux;      // [n]   free for the kernels (per-group scratch)
@@ -222,20 +226,23 @@ struct RouteSmem {
   int* sg_beg;   // [n]   first member (index into members) of each capped group
   int* sg_cnt;   // [n]   member count of each capped group
   int* nsg;      // [1]   number of capped groups
-  int* cnt;      // [E+1] slots per expert (entry E: invalid ids)     (dedup only)
-  int* off;      // [E+1] first member index of each expert           (dedup only)
-  int* wsum;     // [64]  per-warp partial sums of the scan           (dedup only)
 };
 
-// Shared-memory bytes needed by RouteSmem for n slots and E experts.
+// Shared-memory bytes needed by RouteSmem for n slots and E experts.  The
+// base must be 8-byte aligned.
 __host__ __device__ inline int route_smem_bytes(int n, int E, bool dedup) {
-  int ints = 8 * n + 1 + (dedup ? 2 * (E + 1) + 64 : 0);
+  int ints = 8 * n + 1 + (dedup ? 4 * (E + 1) + 64 : 0);
   return ((ints * 4 + 127) / 128) * 128;
 }
 
 __device__ inline RouteSmem route_carve(int* base, int n, int E, bool dedup) {
   RouteSmem r;
   int* p = base;
+  r.mask = dedup ? reinterpret_cast<unsigned long long*>(p) : nullptr;
+  p += dedup ? 2 * (E + 1) : 0;
+  r.cnt = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
+  r.off = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
+  r.wsum = dedup ? p : nullptr; p += dedup ? 64 : 0;
   r.ids = p; p += n;
   r.rank = p; p += n;
   r.aux = p; p += n;
@@ -244,10 +251,7 @@ __device__ inline RouteSmem route_carve(int* base, int n, int E, bool dedup) {
   r.sg_exp = p; p += n;
   r.sg_beg = p; p += n;
   r.sg_cnt = p; p += n;
-  r.nsg = p; p += 1;
-  r.cnt = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
-  r.off = dedup ? p : nullptr; p += dedup ? E + 1 : 0;
-  r.wsum = dedup ? p : nullptr;
+  r.nsg = p;
   return r;
 }
 
@@ -261,30 +265,42 @@ struct NoInit {
 //  * dedup: one group per touched expert, in ascending expert id, members
 //    in slot order, split into groups of at most `cap` members; all invalid
 //    slots form the last group(s) with expert -1.  A stable counting sort:
-//    one warp ranks the slots 32 at a time (match_any), one block-wide scan
-//    places the experts.  Same result in every CTA: deterministic.
+//    with at most 64 tokens and no expert repeated inside a token, each
+//    expert's 64-bit token mask (shared-memory atomicOr) gives every slot
+//    its rank directly; otherwise one warp ranks the slots 32 at a time
+//    (match_any).  One block-wide scan places the experts.  Same result in
+//    every CTA: deterministic.
 //  * no dedup: every slot is its own group (slot order).
-// `init` runs after the id loads are issued and before they are used, so a
-// caller's own set-up (barrier init) overlaps the global-memory latency.
+// `scale` (optional, n floats) is copied to `s_scale` in the same global
+// round trip as the ids.  `init` runs after the loads are issued and before
+// they are used, so a caller's own set-up overlaps their latency.
 // The grouping follows the outputs-not-experts idea of the reference (no
 // align/permute pass over unsorted topk_ids, csrc/moe_gate_up_3d_batched.cu)
 // but shares each expert's weight stream between the slots routed to it.
-template <class Init = NoInit>
+template <bool kScale = false, class Init = NoInit>
 __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict__ topk_ids,
                                    int n, int E, int K, bool dedup, int cap, uint32_t* status,
-                                   Init init = Init()) {
+                                   Init init = Init(), const float* __restrict__ scale = nullptr,
+                                   float* s_scale = nullptr) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int lane = tid & 31, warp = tid >> 5;
-  constexpr int PER = (MAX_SLOTS + 127) / 128;  // ids per thread (blockDim >= 128)
+  constexpr int PER = (MAX_SLOTS + 127) / 128;  // slots per thread (blockDim >= 128)
+  constexpr int SPER = kScale ? PER : 1;
   int ev[PER];
+  float sv[SPER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
     const int i = tid + k * nt;
     ev[k] = i < n ? __ldg(topk_ids + i) : 0;
+    if constexpr (kScale) sv[k] = i < n ? __ldg(scale + i) : 0.f;
   }
   init();
-  if (dedup)
-    for (int e = tid; e <= E; e += nt) r.cnt[e] = 0;
+  if (dedup) {
+    for (int e = tid; e <= E; e += nt) {
+      r.mask[e] = 0ull;
+      r.cnt[e] = 0;
+    }
+  }
   bool bad = false;
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
@@ -293,6 +309,7 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
       int e = ev[k];
       if (e < 0 || e >= E) { e = -1; bad = true; }
       r.ids[i] = e;
+      if constexpr (kScale) s_scale[i] = sv[k];
     }
   }
   if (__syncthreads_or(bad) && tid == 0) raise_status(status, WD_STATUS_BAD_EXPERT_ID);
@@ -308,8 +325,28 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
     __syncthreads();
     return;
   }
-  // Stable rank within each expert (bucket E collects invalid slots).
-  if (warp == 0) {
+  // Token masks; an expert (or the invalid bucket) twice in one token, or
+  // more than 64 tokens, sends the launch to the ordered warp pass.
+  const int ntok = n / K;
+  bool slow = ntok > 64;
+  if (!slow) {
+    for (int i = tid; i < n; i += nt) {
+      const int key = r.ids[i] < 0 ? E : r.ids[i];
+      const int t = i / K;
+      for (int j = t * K; j < i; ++j) slow |= ((r.ids[j] < 0 ? E : r.ids[j]) == key);
+      atomicOr(&r.mask[key], 1ull << t);
+    }
+  }
+  slow = __syncthreads_or(slow);
+  if (!slow) {
+    for (int i = tid; i < n; i += nt) {
+      const int key = r.ids[i] < 0 ? E : r.ids[i];
+      const int t = i / K;
+      r.rank[i] = __popcll(r.mask[key] & ((1ull << t) - 1ull));
+    }
+    for (int e = tid; e <= E; e += nt) r.cnt[e] = __popcll(r.mask[e]);
+  } else if (warp == 0) {
+    // Stable rank within each expert, 32 slots at a time.
     for (int c = 0; c < n; c += 32) {
       const int i = c + lane;
       const bool v = i < n;

@@ -120,8 +120,8 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   for (int i = threadIdx.x; i < a.B * DTC_M; i += blockDim.x) Y[i] = 0.f;
   // h, topk_scale (and possibly topk_ids) come from the preceding kernel.
   pdl_wait_primary();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) s_scale[i] = __ldg(a.scale + i);
-  route_build(r, a.ids, n, a.E, a.K, true, DTC_N, a.status);  // ends with __syncthreads
+  route_build<true>(r, a.ids, n, a.E, a.K, true, DTC_N, a.status, NoInit(), a.scale,
+                    s_scale);  // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nsg = *r.nsg;
@@ -277,30 +277,47 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // Y is final: release it to the cluster, free TMEM meanwhile, then sum the
+  // CL partial tiles in rank order; CTA `rank` writes rows
+  // [rank * 128 / CL, (rank + 1) * 128 / CL) of the tile, 4 rows per thread.
+  if (CL > 1) cluster_arrive();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, DTC_TMEM_COLS);
   }
-  // Sum the CL partial tiles of the cluster in rank order; CTA `rank` writes
-  // rows [rank * 128 / CL, (rank + 1) * 128 / CL) of the tile.
-  if (CL > 1) cluster_sync();
-  const int rpr = DTC_M / CL;
-  for (int i = threadIdx.x; i < a.B * rpr; i += blockDim.x) {
-    const int t = i / rpr, jj = rank * rpr + (i - t * rpr);
-    if (j0 + jj < a.H) {
-      float acc;
-      if (CL > 1) {
-        acc = 0.f;
-        for (int k = 0; k < CL; ++k)
-          acc += dsmem_ld_f32(dsmem_addr(&Y[t * DTC_M + jj], (uint32_t)k));
-      } else {
-        acc = Y[t * DTC_M + jj];
+  if (CL > 1) cluster_wait();
+  const int rpr = DTC_M / CL;   // multiple of 16
+  const int q4 = rpr / 4;
+  for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
+    const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
+    const float* src = &Y[t * DTC_M + jj];
+    float4 acc;
+    if (CL > 1) {
+      float4 part[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < CL) part[k] = dsmem_ld_f32x4(dsmem_addr(src, (uint32_t)k));
+      acc = part[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) {
+        if (k < CL) {
+          acc.x += part[k].x; acc.y += part[k].y; acc.z += part[k].z; acc.w += part[k].w;
+        }
       }
-      if (a.out_fp32)
-        reinterpret_cast<float*>(a.out)[(size_t)t * a.H + j0 + jj] = acc;
-      else
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + j0 + jj] =
-            __float2bfloat16_rn(acc);
+    } else {
+      acc = *reinterpret_cast<const float4*>(src);
+    }
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int row = j0 + jj + u;
+      if (row < a.H) {
+        if (a.out_fp32)
+          reinterpret_cast<float*>(a.out)[(size_t)t * a.H + row] = v[u];
+        else
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + row] =
+              __float2bfloat16_rn(v[u]);
+      }
     }
   }
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
     }
   };
-  route_build(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status, setup);  // ends with __syncthreads
+  route_build<false>(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status, setup);  // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
