@@ -63,6 +63,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="headline only (no per-kernel/e2e legs)")
     p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
+                   help="N > 1: all-reduce fused into the down kernel, or NCCL after it")
     return p.parse_args()
 
 
@@ -211,10 +213,18 @@ def run_ours(args, rank, local_rank, world):
         c.bytes = W.algorithmic_bytes(c.U, B, H, I, K)
         cases[B] = c
 
+    fused = None
+    if world > 1 and args.allreduce == "fused":
+        from warp_decode_b200.tp import FusedAllReduce
+
+        fused = FusedAllReduce(H, max_tokens=64)
+
     def e2e_call(c):
         h = wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids)
         if world == 1:
             return wd.moe_down_3d_batched(h, w_dn, c.ids, c.scale, c.B)
+        if fused is not None:
+            return fused.down(h, w_dn, c.ids, c.scale)
         part = wd.moe_down_3d_batched_partial(h, w_dn, c.ids, c.scale, c.B)
         dist.all_reduce(part)
         return part.to(torch.bfloat16)
@@ -330,7 +340,7 @@ def run_ours(args, rank, local_rank, world):
                     traffic = sum(per) / nB
             except Exception:
                 traffic = None
-        roofline = {"bound": "hbm", "kernel": "moe_gate_up_kernel", "achieved": round(achieved, 1),
+        roofline = {"bound": "hbm", "kernel": "gate_up (moe_gate_up_kernel B<16, moe_gate_up_tc_kernel B>=16)", "achieved": round(achieved, 1),
                     "peak": peak_gbs, "peak_kind": peak_kind, "unit": "GB/s",
                     "frac": round(achieved / peak_gbs, 4),
                     "alg_bytes_per_launch": gu_bytes / nB, "traffic": traffic,
@@ -406,7 +416,9 @@ def run_ours(args, rank, local_rank, world):
             "config": {"workload": WORKLOAD if world == 1 else f"qwen3_235b_inter{I * world}_tp{world}",
                        "hidden": H, "inter_per_gpu": I, "inter_total": I * world, "experts": E,
                        "topk": K, "batches": batches, "global_batch": batches,
-                       "parallelism": "single GPU" if world == 1 else f"tp{world} over inter + NCCL all-reduce",
+                       "parallelism": "single GPU" if world == 1 else (
+                           f"tp{world} over inter + all-reduce fused into the down kernel (NVLink peer stores)"
+                           if fused is not None else f"tp{world} over inter + NCCL all-reduce"),
                        "l2": "flushed before every timed call (256 MiB write + 256 MiB read)",
                        "timing": "CUDA graph replay per call, CUDA events on the launching stream, "
                                  "value = mean us/call over the sweep, max over ranks"},
@@ -422,6 +434,8 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
+        if fused is not None:
+            fused.close()
         dist.destroy_process_group()
     return 0
 

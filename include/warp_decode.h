@@ -155,6 +155,37 @@ WD_API int wd_set_gate_up_path(int path);
  */
 WD_API int wd_set_down_path(int path);
 
+/*
+ * Tensor parallelism over `inter` with the all-reduce fused into down (no
+ * counterpart in the reference, which has no multi-GPU path).  One process
+ * per GPU; every rank of a group of `world` (2..8) ranks:
+ *   1. wd_tp_comm_create(world, rank, max_tokens, hidden, &comm, handle):
+ *      allocates this rank's exchange buffer (2 x world x max_tokens x hidden
+ *      FP32 partials + flags) and writes its 64-byte CUDA IPC handle;
+ *   2. gathers every rank's handle (e.g. all_gather over the process group)
+ *      into an array of world x 64 bytes ordered by rank and calls
+ *      wd_tp_comm_open(comm, handles);
+ *   3. calls wd_moe_down_3d_batched_allreduce instead of
+ *      wd_moe_down_3d_batched + all-reduce: y_out (bf16 [B, hidden]) is the
+ *      sum over all ranks, identical on every rank (ranks added in rank
+ *      order).  Every rank must make the same sequence of calls (same B,
+ *      shapes and order), like a collective, and enter each call within 2 s
+ *      of each other.  Peers exchange rows through
+ *      NVLink peer stores and per-CTA flags; a peer that does not arrive
+ *      within 2 s ends the wait with WD_STATUS_WAIT_TIMEOUT (the output is
+ *      then zeros), never a hang.  Needs the tensor-core down kernel's shapes
+ *      (inter <= 256, E <= 1024) and B <= max_tokens per call chunk.
+ *   4. wd_tp_comm_destroy(comm) after all ranks are done with it.
+ */
+WD_API int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, void** comm,
+                             void* ipc_handle);
+WD_API int wd_tp_comm_open(void* comm, const void* ipc_handles);
+WD_API int wd_tp_comm_destroy(void* comm);
+WD_API int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down,
+                                            const int32_t* topk_ids, const float* topk_scale,
+                                            void* y_out, int B, int E, int topk, int hidden,
+                                            int inter, void* comm, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 10, names
+    assert len(names) == 14, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -34,6 +34,24 @@ def test_gate_up_path_selector_validates():
     assert L.wd_set_down_path(-1) == capi.WD_ERR_SHAPE
     for p in (capi.PATH_SIMT, capi.PATH_TC, capi.PATH_AUTO):
         assert L.wd_set_down_path(p) == capi.WD_OK
+
+
+def test_tp_comm_validates_before_touching_the_device():
+    import ctypes
+
+    L = capi.lib()
+    comm = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(capi.IPC_HANDLE_BYTES)
+    assert L.wd_tp_comm_create(1, 0, 64, 4096, ctypes.byref(comm), handle) == capi.WD_ERR_SHAPE
+    assert L.wd_tp_comm_create(9, 0, 64, 4096, ctypes.byref(comm), handle) == capi.WD_ERR_SHAPE
+    assert L.wd_tp_comm_create(2, 2, 64, 4096, ctypes.byref(comm), handle) == capi.WD_ERR_SHAPE
+    assert L.wd_tp_comm_create(2, 0, 64, 4094, ctypes.byref(comm), handle) == capi.WD_ERR_SHAPE
+    assert L.wd_tp_comm_create(2, 0, 64, 4096, None, handle) == capi.WD_ERR_NULL_POINTER
+    assert L.wd_tp_comm_open(None, handle) == capi.WD_ERR_NULL_POINTER
+    assert L.wd_tp_comm_destroy(None) == capi.WD_OK
+    rc = L.wd_moe_down_3d_batched_allreduce(1, 1, 1, 1, 1, 1, 8, 8, 4096, 192, None, None, None)
+    assert rc == capi.WD_ERR_NULL_POINTER
+    assert b"comm" in L.wd_last_error_message()
 
 
 def test_version_and_error_strings():

@@ -38,7 +38,14 @@ _SIGS = {
     "wd_status_read": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
     "wd_set_gate_up_path": (_I, [_I]),
     "wd_set_down_path": (_I, [_I]),
+    "wd_tp_comm_create": (_I, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "wd_tp_comm_open": (_I, [_P, _P]),
+    "wd_tp_comm_destroy": (_I, [_P]),
+    "wd_moe_down_3d_batched_allreduce": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
+                                              _P]),
 }
+
+IPC_HANDLE_BYTES = 64
 
 # Values of wd_set_gate_up_path / wd_set_down_path.
 GATE_UP_AUTO, GATE_UP_SIMT, GATE_UP_TC = 0, 1, 2
@@ -108,6 +115,37 @@ def set_gate_up_path(path: int) -> None:
 def set_down_path(path: int) -> None:
     """Select the down kernel for later calls (PATH_AUTO / PATH_SIMT / PATH_TC)."""
     check(lib().wd_set_down_path(int(path)))
+
+
+def tp_comm_create(world: int, rank: int, max_tokens: int, hidden: int):
+    """Create this rank's fused-all-reduce communicator; returns (comm, ipc_handle bytes)."""
+    comm = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().wd_tp_comm_create(world, rank, max_tokens, hidden, ctypes.byref(comm), handle))
+    return comm.value, handle.raw
+
+
+def tp_comm_open(comm: int, handles: bytes) -> None:
+    """Open the peers' buffers; `handles` = every rank's handle, in rank order."""
+    buf = ctypes.create_string_buffer(handles, len(handles))
+    check(lib().wd_tp_comm_open(comm, buf))
+
+
+def tp_comm_destroy(comm: int) -> None:
+    check(lib().wd_tp_comm_destroy(comm))
+
+
+def torch_down_allreduce(h, w, ids, scale, comm):
+    """bf16 y[B, hidden] = sum over the group's ranks of down(h_r) (fused all-reduce)."""
+    import torch
+
+    B, K = ids.shape
+    E, H, I = w.shape
+    y = torch.empty(B, H, dtype=torch.bfloat16, device=h.device)
+    check(lib().wd_moe_down_3d_batched_allreduce(h.data_ptr(), w.data_ptr(), ids.data_ptr(),
+                                                 scale.data_ptr(), y.data_ptr(), B, E, K, H, I,
+                                                 comm, None, _stream()))
+    return y
 
 
 def status_read(clear: bool = True) -> int:

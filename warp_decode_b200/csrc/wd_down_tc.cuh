@@ -41,6 +41,20 @@ constexpr int DTC_A_CHUNK = DTC_M * DTC_BK * 2;  // 16 KB of weights
 constexpr int DTC_B_CHUNK = DTC_N * DTC_BK * 2;  // 2 KB of h rows
 constexpr uint32_t DTC_TMEM_COLS = DTC_ND * DTC_N < 32 ? 32 : DTC_ND * DTC_N;
 
+// Fused one-shot all-reduce over the ranks of a tensor-parallel group (one
+// process per GPU, peer memory opened through CUDA IPC).  Every rank's
+// buffer holds [2 slots][world][max_tokens][H] FP32 partials and
+// [world][max_ctas] flags; epochs[cta] counts this rank's calls per CTA.
+constexpr int TP_MAX_WORLD = 8;
+struct TpArgs {
+  int world;                        // <= 1: no fused all-reduce
+  int rank;
+  int max_tokens, max_ctas;
+  float* recv[TP_MAX_WORLD];        // partial buffers of every rank (peer pointers)
+  uint32_t* flags[TP_MAX_WORLD];    // flag arrays of every rank (peer pointers)
+  uint32_t* epochs;                 // this rank's per-CTA call counters
+};
+
 struct DownTcArgs {
   const __nv_bfloat16* h;  // [B*K, I]
   const int32_t* ids;      // [B, K]
@@ -52,6 +66,7 @@ struct DownTcArgs {
   int stages;              // weight ring depth
   int nbuf;                // h buffers, >= DTC_GW
   int cl;                  // CTAs per cluster (1, 2, 4 or 8)
+  TpArgs tp;               // fused all-reduce (tp.world > 1): out = bf16 sum over ranks
 };
 
 __host__ __device__ inline int down_tc_kc(int I) { return (I + DTC_BK - 1) / DTC_BK; }
@@ -288,6 +303,12 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   if (CL > 1) cluster_wait();
   const int rpr = DTC_M / CL;   // multiple of 16
   const int q4 = rpr / 4;
+  const bool tp = a.tp.world > 1;
+  const uint32_t ep = tp ? a.tp.epochs[blockIdx.x] + 1u : 0u;  // this call's epoch
+  const int slot = (int)(ep & 1u);
+  auto recv_at = [&](const float* buf, int src, int t, int row) {
+    return buf + (((size_t)(slot * a.tp.world + src) * a.tp.max_tokens + t) * a.H + row);
+  };
   for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
     const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
     const float* src = &Y[t * DTC_M + jj];
@@ -308,6 +329,20 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       acc = *reinterpret_cast<const float4*>(src);
     }
     const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (tp) {
+      // Push this rank's partial rows into slot `slot` of every rank's buffer.
+      for (int r = 0; r < a.tp.world; ++r) {
+        float* dst = const_cast<float*>(recv_at(a.tp.recv[r], a.tp.rank, t, j0 + jj));
+        if (j0 + jj + 3 < a.H) {
+          *reinterpret_cast<float4*>(dst) = acc;
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (j0 + jj + u < a.H) dst[u] = v[u];
+        }
+      }
+      continue;
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int row = j0 + jj + u;
@@ -321,6 +356,48 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     }
   }
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile
+  if (tp) {
+    // Publish this CTA's rows to every rank, wait for every rank's rows of
+    // the same CTA (bounded), then sum them in rank order.
+    __shared__ int s_tp_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < a.tp.world; ++r)
+        st_release_sys(a.tp.flags[r] + (size_t)a.tp.rank * a.tp.max_ctas + blockIdx.x, ep);
+      const uint32_t* mine = a.tp.flags[a.tp.rank];
+      bool ok = true;
+      for (int r = 0; r < a.tp.world && ok; ++r) {
+        const uint32_t* f = mine + (size_t)r * a.tp.max_ctas + blockIdx.x;
+        const uint64_t t0 = globaltimer_ns();
+        while ((int32_t)(ld_acquire_sys(f) - ep) < 0) {
+          if (globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            ok = false;
+            break;
+          }
+        }
+      }
+      a.tp.epochs[blockIdx.x] = ep;
+      s_tp_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    const float* mine = a.tp.recv[a.tp.rank];
+    for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
+      const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = j0 + jj + u;
+        if (row < a.H) {
+          float acc = 0.f;
+          if (s_tp_ok)
+            for (int r = 0; r < a.tp.world; ++r) acc += *recv_at(mine, r, t, row);
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + row] =
+              __float2bfloat16_rn(acc);
+        }
+      }
+    }
+  }
 }
 
 }  // namespace wdb

@@ -368,7 +368,8 @@ bool down_tc_applies(int B, int E, int hidden, int inter, int sms) {
 // fall back to the SIMT kernel.
 int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const int32_t* ids,
                    const float* scale, void* out, int out_fp32, int bn, int E, int topk,
-                   int hidden, int inter, uint32_t* status, cudaStream_t s) {
+                   int hidden, int inter, uint32_t* status, cudaStream_t s,
+                   const wdb::TpArgs* tp = nullptr) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   // w_down [E, H, I]: box = 64 K-columns of 128 rows of one expert.
@@ -402,6 +403,12 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   a.stages = stages;
   a.nbuf = nbuf;
   a.cl = cl;
+  a.tp = {};
+  if (tp) {
+    if (((hidden + wdb::DTC_M - 1) / wdb::DTC_M) * cl > tp->max_ctas)
+      return fail(WD_ERR_UNSUPPORTED, "grid larger than the communicator's flag array");
+    a.tp = *tp;
+  }
   cudaLaunchAttribute attr[2];
   int na = 0;
   if (cl > 1) {
@@ -527,6 +534,16 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
   return WD_OK;
 }
 
+// ---- tensor-parallel communicator for the fused all-reduce ------------------
+struct TpComm {
+  int device = -1;
+  int world = 0, rank = 0, max_tokens = 0, hidden = 0, max_ctas = 0;
+  void* block = nullptr;          // [2][world][max_tokens][hidden] f32, then flags
+  size_t recv_bytes = 0;
+  uint32_t* epochs = nullptr;     // [max_ctas], local only
+  void* peer[wdb::TP_MAX_WORLD] = {};  // opened IPC mappings (nullptr for self)
+};
+
 }  // namespace
 
 extern "C" {
@@ -592,6 +609,116 @@ int wd_set_down_path(int path) {
   g_last_error.clear();
   if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
   g_down_path.store(path);
+  return WD_OK;
+}
+
+int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, void** comm,
+                      void* ipc_handle) {
+  g_last_error.clear();
+  if (!comm || !ipc_handle) return fail(WD_ERR_NULL_POINTER, "comm and ipc_handle are required");
+  *comm = nullptr;
+  if (world < 2 || world > wdb::TP_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(WD_ERR_SHAPE, "world must be 2..8 and 0 <= rank < world");
+  if (max_tokens < 1 || hidden < 4 || hidden % 4 != 0)
+    return fail(WD_ERR_SHAPE, "max_tokens >= 1 and hidden % 4 == 0 required");
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  TpComm* c = new TpComm();
+  cudaGetDevice(&c->device);
+  c->world = world; c->rank = rank; c->max_tokens = max_tokens; c->hidden = hidden;
+  c->max_ctas = dev->sm_count;
+  c->recv_bytes = ((size_t)2 * world * max_tokens * hidden * 4 + 255) / 256 * 256;
+  const size_t flag_bytes = (size_t)world * c->max_ctas * 4;
+  cudaError_t err = cudaMalloc(&c->block, c->recv_bytes + flag_bytes);
+  if (err == cudaSuccess) err = cudaMemset(c->block, 0, c->recv_bytes + flag_bytes);
+  if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->max_ctas * 4);
+  if (err == cudaSuccess) err = cudaMemset(c->epochs, 0, c->max_ctas * 4);
+  if (err == cudaSuccess)
+    err = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), c->block);
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) {
+    if (c->block) cudaFree(c->block);
+    if (c->epochs) cudaFree(c->epochs);
+    delete c;
+    return fail(WD_ERR_CUDA, std::string("tp comm create: ") + cudaGetErrorString(err));
+  }
+  *comm = c;
+  return WD_OK;
+}
+
+int wd_tp_comm_open(void* comm, const void* ipc_handles) {
+  g_last_error.clear();
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (!c || !ipc_handles) return fail(WD_ERR_NULL_POINTER, "comm and ipc_handles are required");
+  const auto* hs = static_cast<const cudaIpcMemHandle_t*>(ipc_handles);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank || c->peer[r]) continue;
+    const cudaError_t err =
+        cudaIpcOpenMemHandle(&c->peer[r], hs[r], cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess)
+      return fail(WD_ERR_CUDA, std::string("tp comm open (rank ") + std::to_string(r) +
+                                   "): " + cudaGetErrorString(err));
+  }
+  return WD_OK;
+}
+
+int wd_tp_comm_destroy(void* comm) {
+  g_last_error.clear();
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (!c) return WD_OK;
+  cudaDeviceSynchronize();
+  for (int r = 0; r < c->world; ++r)
+    if (c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]);
+  cudaFree(c->block);
+  cudaFree(c->epochs);
+  delete c;
+  return WD_OK;
+}
+
+int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const int32_t* topk_ids,
+                                     const float* topk_scale, void* y_out, int B, int E, int topk,
+                                     int hidden, int inter, void* comm, uint32_t* status,
+                                     void* stream) {
+  g_last_error.clear();
+  TpComm* c = static_cast<TpComm*>(comm);
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (!c) return fail(WD_ERR_NULL_POINTER, "comm is NULL");
+  if (B == 0) return WD_OK;
+  if (!h || !w_down || !topk_ids || !topk_scale || !y_out)
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(h) || !aligned16(w_down) || inter % 8 != 0)
+    return fail(WD_ERR_ALIGNMENT, "h and w_down must be 16-byte aligned, inter % 8 == 0");
+  if (hidden != c->hidden) return fail(WD_ERR_SHAPE, "hidden differs from the communicator's");
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && !c->peer[r]) return fail(WD_ERR_UNSUPPORTED, "communicator not opened");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK ||
+      (hidden + wdb::DTC_M - 1) / wdb::DTC_M > dev->sm_count)
+    return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 256)");
+  wdb::TpArgs tp = {};
+  tp.world = c->world;
+  tp.rank = c->rank;
+  tp.max_tokens = c->max_tokens;
+  tp.max_ctas = c->max_ctas;
+  tp.epochs = c->epochs;
+  for (int r = 0; r < c->world; ++r) {
+    uint8_t* base = static_cast<uint8_t*>(r == c->rank ? c->block : c->peer[r]);
+    tp.recv[r] = reinterpret_cast<float*>(base);
+    tp.flags[r] = reinterpret_cast<uint32_t*>(base + c->recv_bytes);
+  }
+  const int tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), std::min(64, c->max_tokens));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < B; b0 += tb) {
+    const int bn = std::min(tb, B - b0);
+    rc = down_tc_launch(dev, reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter,
+                        w_down, topk_ids + (size_t)b0 * topk, topk_scale + (size_t)b0 * topk,
+                        reinterpret_cast<__nv_bfloat16*>(y_out) + (size_t)b0 * hidden, 0, bn, E,
+                        topk, hidden, inter, status, s, &tp);
+    if (rc) return rc;
+  }
   return WD_OK;
 }
 

@@ -10,7 +10,9 @@ benchmark/bench.py:307-310 of Religious-J/warp_decode divides inter by
 * x, topk_ids and topk_scale are replicated;
 * gate_up needs no communication; down produces an FP32 partial [B, hidden]
   (no bf16 rounding before the sum), followed by ONE all-reduce (NCCL over
-  NVLink on GPUs) and a single bf16 rounding.
+  NVLink on GPUs) and a single bf16 rounding -- or, with FusedAllReduce, the
+  down kernel itself pushes its FP32 rows to every rank over NVLink and sums
+  the ranks' rows in rank order (one kernel, no NCCL launch).
 
 Because silu(gate)*up is elementwise in the intermediate dimension and down
 is linear in it, sum_r down_r(gate_up_r(x)) equals the unsharded FFN up to
@@ -68,6 +70,36 @@ class CudaKernels:
         return self.wd.moe_down_3d_batched_mxfp8(h, w, w_scale, ids, scale, B, True)
 
 
+class FusedAllReduce:
+    """The fused all-reduce of the tensor-core down kernel for one process group.
+
+    Collective to construct (every rank at once): each rank allocates its
+    exchange buffer, the CUDA IPC handles are all-gathered over `group`, and
+    every rank maps its peers' buffers.  Then ``down(h, w, ids, scale)``
+    returns the bf16 sum over ranks directly (no NCCL call, no cast kernel).
+    """
+
+    def __init__(self, hidden: int, max_tokens: int = 64, group=None):
+        from . import capi
+
+        self.capi = capi
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.hidden = hidden
+        self.comm, handle = capi.tp_comm_create(self.world, self.rank, max_tokens, hidden)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        capi.tp_comm_open(self.comm, b"".join(handles))
+
+    def down(self, h, w, ids, scale):
+        return self.capi.torch_down_allreduce(h, w, ids, scale, self.comm)
+
+    def close(self):
+        if self.comm:
+            self.capi.tp_comm_destroy(self.comm)
+            self.comm = None
+
+
 class TensorParallelMoE:
     """One rank's share of a tensor-parallel MoE FFN (decode).
 
@@ -79,8 +111,10 @@ class TensorParallelMoE:
 
     def __init__(self, w_gate_up, w_down, *, rank: Optional[int] = None,
                  world: Optional[int] = None, group=None, w_gate_up_scale=None,
-                 w_down_scale=None, presharded: bool = False, kernels=None):
+                 w_down_scale=None, presharded: bool = False, kernels=None,
+                 fused: Optional[FusedAllReduce] = None):
         self.group = group
+        self.fused = fused
         if world is None:
             world = dist.get_world_size(group) if dist.is_initialized() else 1
         if rank is None:
@@ -107,6 +141,9 @@ class TensorParallelMoE:
         return self.kernels.down_partial(h, self.w_dn, topk_ids, topk_scale, B, self.s_dn)
 
     def __call__(self, x, topk_ids, topk_scale):
+        if self.fused is not None and self.world > 1 and self.s_dn is None:
+            h = self.kernels.gate_up(x, self.w_gu, topk_ids, self.s_gu)
+            return self.fused.down(h, self.w_dn, topk_ids, topk_scale)
         part = self.partial(x, topk_ids, topk_scale)
         if self.world > 1:
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
