@@ -161,7 +161,8 @@ WD_API int wd_set_down_path(int path);
  * per GPU; every rank of a group of `world` (2..8) ranks:
  *   1. wd_tp_comm_create(world, rank, max_tokens, hidden, &comm, handle):
  *      allocates this rank's exchange buffer (2 x world x max_tokens x hidden
- *      FP32 partials + flags) and writes its 64-byte CUDA IPC handle;
+ *      8-byte packets: FP32 partial + call epoch) and writes its 64-byte CUDA
+ *      IPC handle;
  *   2. gathers every rank's handle (e.g. all_gather over the process group)
  *      into an array of world x 64 bytes ordered by rank and calls
  *      wd_tp_comm_open(comm, handles);
@@ -170,8 +171,8 @@ WD_API int wd_set_down_path(int path);
  *      sum over all ranks, identical on every rank (ranks added in rank
  *      order).  Every rank must make the same sequence of calls (same B,
  *      shapes and order), like a collective, and enter each call within 2 s
- *      of each other.  Peers exchange rows through
- *      NVLink peer stores and per-CTA flags; a peer that does not arrive
+ *      of each other.  Peers exchange rows as epoch-tagged packets through
+ *      NVLink peer stores (no fences, no flags); a peer that does not arrive
  *      within 2 s ends the wait with WD_STATUS_WAIT_TIMEOUT (the output is
  *      then zeros), never a hang.  Needs the tensor-core down kernel's shapes
  *      (inter <= 256, E <= 1024) and B <= max_tokens per call chunk.

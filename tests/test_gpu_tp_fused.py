@@ -2,7 +2,7 @@
 
 Two processes on two GPUs (skipped with fewer): each rank holds half of the
 intermediate dimension of a Qwen3-235B-style FFN; the fused path
-(FusedAllReduce: peer stores + per-CTA flags inside the down kernel) must
+(FusedAllReduce: epoch-tagged packets pushed to every rank by the down kernel) must
 match the NCCL path and the unsharded FP32 oracle (rtol = atol = 1e-2), give
 bitwise-identical outputs on both ranks, survive CUDA-graph replay (epochs
 advance), and end a wait whose peer never arrives with WD_STATUS_WAIT_TIMEOUT

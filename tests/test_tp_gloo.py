@@ -128,3 +128,65 @@ def test_missing_rank_times_out_instead_of_hanging():
     out = q.get(timeout=90)
     p.join(timeout=30)
     assert out != "joined"
+
+
+class _FakeCapi:
+    """Records what FusedAllReduce asks of the C ABI (no GPU)."""
+
+    def __init__(self):
+        self.calls = []
+
+    def tp_comm_create(self, world, rank, max_tokens, hidden):
+        self.calls.append(("create", world, rank, max_tokens, hidden))
+        return 1000 + rank, bytes([rank]) * 64
+
+    def tp_comm_open(self, comm, handles):
+        self.calls.append(("open", comm, handles))
+
+    def torch_down_allreduce(self, h, w, ids, scale, comm):
+        self.calls.append(("down", comm))
+        return "y"
+
+    def tp_comm_destroy(self, comm):
+        self.calls.append(("destroy", comm))
+
+
+def _fused_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from warp_decode_b200.tp import FusedAllReduce
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=30))
+    fake = _FakeCapi()
+    f = FusedAllReduce(4096, max_tokens=32, _capi=fake)
+    out = f.down(None, None, None, None)
+    f.close()
+    f.close()  # idempotent
+    dist.destroy_process_group()
+    q.put((rank, fake.calls, out))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_allreduce_handle_exchange(world):
+    """Every rank creates its communicator, opens all ranks' IPC handles in
+    rank order, calls the fused down with its own communicator and destroys
+    it once."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict((r, (c, o)) for r, c, o in (q.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+    expected_handles = b"".join(bytes([r]) * 64 for r in range(world))
+    for r in range(world):
+        calls, out = res[r]
+        assert calls[0] == ("create", world, r, 32, 4096)
+        assert calls[1] == ("open", 1000 + r, expected_handles)
+        assert calls[2] == ("down", 1000 + r)
+        assert calls[3:] == [("destroy", 1000 + r)]
+        assert out == "y"

@@ -43,17 +43,28 @@ constexpr uint32_t DTC_TMEM_COLS = DTC_ND * DTC_N < 32 ? 32 : DTC_ND * DTC_N;
 
 // Fused one-shot all-reduce over the ranks of a tensor-parallel group (one
 // process per GPU, peer memory opened through CUDA IPC).  Every rank's
-// buffer holds [2 slots][world][max_tokens][H] FP32 partials and
-// [world][max_ctas] flags; epochs[cta] counts this rank's calls per CTA.
+// buffer holds [2 slots][world][max_tokens][H] packets of 8 bytes: the FP32
+// partial and the epoch of the call that wrote it, stored together by one
+// 8-byte store, so a reader that sees the epoch sees the value (no fences,
+// no separate flags).  epochs[cta] counts this rank's calls per CTA; slot =
+// epoch & 1 keeps a rank that is one call ahead off the slot still being read.
 constexpr int TP_MAX_WORLD = 8;
 struct TpArgs {
   int world;                        // <= 1: no fused all-reduce
   int rank;
   int max_tokens, max_ctas;
-  float* recv[TP_MAX_WORLD];        // partial buffers of every rank (peer pointers)
-  uint32_t* flags[TP_MAX_WORLD];    // flag arrays of every rank (peer pointers)
+  uint2* recv[TP_MAX_WORLD];        // packet buffers of every rank (peer pointers)
   uint32_t* epochs;                 // this rank's per-CTA call counters
 };
+
+__device__ __forceinline__ void st_volatile_u2(uint2* p, uint32_t a, uint32_t b) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ uint2 ld_volatile_u2(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
 
 struct DownTcArgs {
   const __nv_bfloat16* h;  // [B*K, I]
@@ -108,6 +119,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int rank = CL > 1 ? (int)cluster_ctarank() : 0;
   const int j0 = ((int)blockIdx.x / CL) * DTC_M;
+  const uint32_t tp_ep = a.tp.world > 1 ? a.tp.epochs[blockIdx.x] + 1u : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -304,11 +316,12 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int rpr = DTC_M / CL;   // multiple of 16
   const int q4 = rpr / 4;
   const bool tp = a.tp.world > 1;
-  const uint32_t ep = tp ? a.tp.epochs[blockIdx.x] + 1u : 0u;  // this call's epoch
+  const uint32_t ep = tp_ep;  // this call's epoch (read at kernel start)
   const int slot = (int)(ep & 1u);
-  auto recv_at = [&](const float* buf, int src, int t, int row) {
+  auto recv_at = [&](uint2* buf, int src, int t, int row) {
     return buf + (((size_t)(slot * a.tp.world + src) * a.tp.max_tokens + t) * a.H + row);
   };
+  bool tp_ok = true;
   for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
     const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
     const float* src = &Y[t * DTC_M + jj];
@@ -330,16 +343,44 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     }
     const float v[4] = {acc.x, acc.y, acc.z, acc.w};
     if (tp) {
-      // Push this rank's partial rows into slot `slot` of every rank's buffer.
+      // Push (value, epoch) packets of this rank's rows to every rank, then
+      // collect every rank's packets of the same rows and add them in rank
+      // order.  A packet that does not arrive within the bound counts as 0
+      // and raises WD_STATUS_WAIT_TIMEOUT.
       for (int r = 0; r < a.tp.world; ++r) {
-        float* dst = const_cast<float*>(recv_at(a.tp.recv[r], a.tp.rank, t, j0 + jj));
-        if (j0 + jj + 3 < a.H) {
-          *reinterpret_cast<float4*>(dst) = acc;
-        } else {
+        uint2* dst = recv_at(a.tp.recv[r], a.tp.rank, t, j0 + jj);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (j0 + jj + u < a.H) dst[u] = v[u];
+        for (int u = 0; u < 4; ++u)
+          if (j0 + jj + u < a.H) st_volatile_u2(dst + u, __float_as_uint(v[u]), ep);
+      }
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      uint2* mine = a.tp.recv[a.tp.rank];
+      for (int r = 0; r < a.tp.world; ++r) {
+        const uint2* p = recv_at(mine, r, t, j0 + jj);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (j0 + jj + u >= a.H || !tp_ok) continue;
+          uint2 pk = ld_volatile_u2(p + u);
+          if (pk.y != ep) {
+            const uint64_t t0 = globaltimer_ns();
+            do {
+              pk = ld_volatile_u2(p + u);
+              if (pk.y != ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+                raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+                tp_ok = false;
+                break;
+              }
+            } while (pk.y != ep);
+          }
+          if (tp_ok) sum[u] += __uint_as_float(pk.x);
         }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = j0 + jj + u;
+        if (row < a.H)
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + row] =
+              __float2bfloat16_rn(tp_ok ? sum[u] : 0.f);
       }
       continue;
     }
@@ -355,49 +396,8 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       }
     }
   }
+  if (tp && threadIdx.x == 0) a.tp.epochs[blockIdx.x] = ep;
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile
-  if (tp) {
-    // Publish this CTA's rows to every rank, wait for every rank's rows of
-    // the same CTA (bounded), then sum them in rank order.
-    __shared__ int s_tp_ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int r = 0; r < a.tp.world; ++r)
-        st_release_sys(a.tp.flags[r] + (size_t)a.tp.rank * a.tp.max_ctas + blockIdx.x, ep);
-      const uint32_t* mine = a.tp.flags[a.tp.rank];
-      bool ok = true;
-      for (int r = 0; r < a.tp.world && ok; ++r) {
-        const uint32_t* f = mine + (size_t)r * a.tp.max_ctas + blockIdx.x;
-        const uint64_t t0 = globaltimer_ns();
-        while ((int32_t)(ld_acquire_sys(f) - ep) < 0) {
-          if (globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
-            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-            ok = false;
-            break;
-          }
-        }
-      }
-      a.tp.epochs[blockIdx.x] = ep;
-      s_tp_ok = ok ? 1 : 0;
-    }
-    __syncthreads();
-    const float* mine = a.tp.recv[a.tp.rank];
-    for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
-      const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = j0 + jj + u;
-        if (row < a.H) {
-          float acc = 0.f;
-          if (s_tp_ok)
-            for (int r = 0; r < a.tp.world; ++r) acc += *recv_at(mine, r, t, row);
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + row] =
-              __float2bfloat16_rn(acc);
-        }
-      }
-    }
-  }
 }
 
 }  // namespace wdb

@@ -406,7 +406,7 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   a.tp = {};
   if (tp) {
     if (((hidden + wdb::DTC_M - 1) / wdb::DTC_M) * cl > tp->max_ctas)
-      return fail(WD_ERR_UNSUPPORTED, "grid larger than the communicator's flag array");
+      return fail(WD_ERR_UNSUPPORTED, "grid larger than the communicator's epoch array");
     a.tp = *tp;
   }
   cudaLaunchAttribute attr[2];
@@ -538,7 +538,7 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
 struct TpComm {
   int device = -1;
   int world = 0, rank = 0, max_tokens = 0, hidden = 0, max_ctas = 0;
-  void* block = nullptr;          // [2][world][max_tokens][hidden] f32, then flags
+  void* block = nullptr;          // [2][world][max_tokens][hidden] 8-byte packets
   size_t recv_bytes = 0;
   uint32_t* epochs = nullptr;     // [max_ctas], local only
   void* peer[wdb::TP_MAX_WORLD] = {};  // opened IPC mappings (nullptr for self)
@@ -628,10 +628,9 @@ int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, void** co
   cudaGetDevice(&c->device);
   c->world = world; c->rank = rank; c->max_tokens = max_tokens; c->hidden = hidden;
   c->max_ctas = dev->sm_count;
-  c->recv_bytes = ((size_t)2 * world * max_tokens * hidden * 4 + 255) / 256 * 256;
-  const size_t flag_bytes = (size_t)world * c->max_ctas * 4;
-  cudaError_t err = cudaMalloc(&c->block, c->recv_bytes + flag_bytes);
-  if (err == cudaSuccess) err = cudaMemset(c->block, 0, c->recv_bytes + flag_bytes);
+  c->recv_bytes = ((size_t)2 * world * max_tokens * hidden * 8 + 255) / 256 * 256;
+  cudaError_t err = cudaMalloc(&c->block, c->recv_bytes);
+  if (err == cudaSuccess) err = cudaMemset(c->block, 0, c->recv_bytes);
   if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&c->epochs), c->max_ctas * 4);
   if (err == cudaSuccess) err = cudaMemset(c->epochs, 0, c->max_ctas * 4);
   if (err == cudaSuccess)
@@ -704,11 +703,8 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
   tp.max_tokens = c->max_tokens;
   tp.max_ctas = c->max_ctas;
   tp.epochs = c->epochs;
-  for (int r = 0; r < c->world; ++r) {
-    uint8_t* base = static_cast<uint8_t*>(r == c->rank ? c->block : c->peer[r]);
-    tp.recv[r] = reinterpret_cast<float*>(base);
-    tp.flags[r] = reinterpret_cast<uint32_t*>(base + c->recv_bytes);
-  }
+  for (int r = 0; r < c->world; ++r)
+    tp.recv[r] = static_cast<uint2*>(r == c->rank ? c->block : c->peer[r]);
   const int tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), std::min(64, c->max_tokens));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {

@@ -11,8 +11,9 @@ benchmark/bench.py:307-310 of Religious-J/warp_decode divides inter by
 * gate_up needs no communication; down produces an FP32 partial [B, hidden]
   (no bf16 rounding before the sum), followed by ONE all-reduce (NCCL over
   NVLink on GPUs) and a single bf16 rounding -- or, with FusedAllReduce, the
-  down kernel itself pushes its FP32 rows to every rank over NVLink and sums
-  the ranks' rows in rank order (one kernel, no NCCL launch).
+  down kernel itself pushes its FP32 rows to every rank over NVLink as
+  epoch-tagged 8-byte packets and sums the ranks' rows in rank order (one
+  kernel, no NCCL launch, no fences).
 
 Because silu(gate)*up is elementwise in the intermediate dimension and down
 is linear in it, sum_r down_r(gate_up_r(x)) equals the unsharded FFN up to
@@ -79,9 +80,11 @@ class FusedAllReduce:
     returns the bf16 sum over ranks directly (no NCCL call, no cast kernel).
     """
 
-    def __init__(self, hidden: int, max_tokens: int = 64, group=None):
-        from . import capi
+    def __init__(self, hidden: int, max_tokens: int = 64, group=None, _capi=None):
+        if _capi is None:
+            from . import capi as _capi
 
+        capi = _capi
         self.capi = capi
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
