@@ -223,7 +223,7 @@ def run_ours(args, rank, local_rank, world):
         h = wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids)
         if world == 1:
             return wd.moe_down_3d_batched(h, w_dn, c.ids, c.scale, c.B)
-        if fused is not None:
+        if fused is not None and fused.applies(c.B):
             return fused.down(h, w_dn, c.ids, c.scale)
         part = wd.moe_down_3d_batched_partial(h, w_dn, c.ids, c.scale, c.B)
         dist.all_reduce(part)
@@ -417,7 +417,8 @@ def run_ours(args, rank, local_rank, world):
                        "hidden": H, "inter_per_gpu": I, "inter_total": I * world, "experts": E,
                        "topk": K, "batches": batches, "global_batch": batches,
                        "parallelism": "single GPU" if world == 1 else (
-                           f"tp{world} over inter + all-reduce fused into the down kernel (NVLink peer stores)"
+                           f"tp{world} over inter + all-reduce fused into the down kernel (NVLink peer stores) "
+                           f"for B <= {max([B for B in batches if fused.applies(B)], default=0)}, NCCL above"
                            if fused is not None else f"tp{world} over inter + NCCL all-reduce"),
                        "l2": "flushed before every timed call (256 MiB write + 256 MiB read)",
                        "timing": "CUDA graph replay per call, CUDA events on the launching stream, "
