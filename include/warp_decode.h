@@ -99,10 +99,10 @@ WD_API int wd_moe_gate_up_3d_batched(const void* x, const void* w_gate_up,
  * FP32 products and accumulation.  out_fp32 = 0 writes bf16, 1 writes fp32
  * (un-rounded tensor-parallel partial sums).  Requirements: inter % 8 == 0,
  * 1 <= topk <= 512, h / w_down 16-byte aligned.
- * The launch may start early behind a directly preceding
- * wd_moe_gate_up_3d_batched on the same stream (programmatic dependent
- * launch) and prefetch w_down rows; it reads h and topk_scale only after the
- * preceding kernel has finished, and re-checks topk_ids then.
+ * With WARP_DECODE_PDL=1 the launch may start early behind a directly
+ * preceding wd_moe_gate_up_3d_batched on the same stream (programmatic
+ * dependent launch) and prefetch w_down rows; it reads h and topk_scale only
+ * after the preceding kernel has finished, and re-checks topk_ids then.
  * Replaces warp_decode::launch_moe_down_3d_batched (csrc/moe_down_3d_batched.cu:124-141).
  */
 WD_API int wd_moe_down_3d_batched(const void* h, const void* w_down,

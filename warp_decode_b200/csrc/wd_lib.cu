@@ -86,10 +86,15 @@ int device_info(DeviceInfo** out) {
   return WD_OK;
 }
 
+// Programmatic dependent launch of down behind gate_up: opt-in
+// (WARP_DECODE_PDL=1).  Measured on B200 with CUDA-graph replay, the early
+// start made the pair slower (B=2: 43.1 vs 35.0 us, B=4: 53.5 vs 47.1 us):
+// the down CTAs cannot share an SM with a gate_up CTA (shared memory), and
+// the early-launched grid delays its clusters.
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("WARP_DECODE_PDL");
-    return !(v && v[0] == '0');
+    return v && v[0] == '1';
   }();
   return on;
 }
