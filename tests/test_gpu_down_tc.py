@@ -90,9 +90,11 @@ def test_qwen3_tp8_both_paths(wd, B):
     (5, 6, 6, 128, 64, "randint"),      # repeated ids inside a token (fixed add order)
     (100, 64, 8, 512, 64, "uniform"),   # B*topk > 512: two launches
     (4, 2048, 8, 256, 64, "uniform"),   # E > 1024: SIMT path
-    (2, 16, 4, 512, 1544, "uniform"),   # inter > 256: SIMT path
+    (2, 16, 4, 512, 1544, "uniform"),   # inter > 1024: SIMT path
+    (6, 16, 4, 512, 1000, "uniform"),   # 16 K chunks over 4 weight stages, last chunk partial
+    (9, 32, 8, 1024, 512, "randint"),   # 2 weight stages per item, repeated ids
     (8, 256, 8, 7168, 256, "zipf"),     # DeepSeek-V3 TP=8 shard: 56 tiles, clusters of 2
-    (16, 128, 8, 2048, 768, "uniform"), # Qwen3-30B shape, bf16 (SIMT: inter > 256)
+    (16, 128, 8, 2048, 768, "uniform"), # Qwen3-30B shape, bf16: 3 weight stages per item
 ])
 def test_shapes_tc(wd, B, E, K, H, I, routing):
     inp = W.make_host_inputs(B, H, I, E, K, seed=B * 13 + E, routing=routing, full=True)

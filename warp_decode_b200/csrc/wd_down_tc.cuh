@@ -12,7 +12,8 @@
 //    deterministic.
 //  * Per item (one expert, at most DTC_N of its routed slots):
 //      A = the expert's 128 weight rows of the tile (M = 128, K = inter),
-//          one 3-D TMA box per 64-wide K chunk (16 KB each);
+//          one 3-D TMA box per 64-wide K chunk (16 KB each), up to 4
+//          chunks per ring stage (inter up to 1024: several stages);
 //      B = the members' h rows (N = 16), gathered by the gather warps into
 //          the 128-byte-swizzled K-major layout;
 //      D[j, c] (TMEM lane j, column c) = row j . h[member c].
@@ -32,7 +33,8 @@ namespace wdb {
 
 constexpr int DTC_M = 128;                       // output rows per tile (MMA M)
 constexpr int DTC_BK = 64;                       // K elements per chunk (128-byte rows)
-constexpr int DTC_MAXKC = 4;                     // inter <= 256
+constexpr int DTC_MAXKC = 16;                    // inter <= 1024
+constexpr int DTC_SC = 4;                        // max K chunks per weight stage
 constexpr int DTC_N = 16;                        // members per item (MMA N)
 constexpr int DTC_ND = 4;                        // TMEM accumulator buffers
 constexpr int DTC_GW = 4;                        // gather warps
@@ -75,16 +77,18 @@ struct DownTcArgs {
   uint32_t* status;
   int B, E, K, H, I;
   int stages;              // weight ring depth
-  int nbuf;                // h buffers, >= DTC_GW
+  int sc;                  // K chunks per weight stage (<= DTC_SC)
+  int nbuf;                // h buffers, >= DTC_GW (a gather warp is at most one
+                           // ring turn ahead, so mbarrier parities cannot alias)
   int cl;                  // CTAs per cluster (1, 2, 4 or 8)
   TpArgs tp;               // fused all-reduce (tp.world > 1): out = bf16 sum over ranks
 };
 
 __host__ __device__ inline int down_tc_kc(int I) { return (I + DTC_BK - 1) / DTC_BK; }
 
-__host__ inline int down_tc_smem_bytes(int stages, int nbuf, int I, int B, int n, int E) {
+__host__ inline int down_tc_smem_bytes(int stages, int sc, int nbuf, int I, int B, int n, int E) {
   const int kc = down_tc_kc(I);
-  return 1024 + stages * kc * DTC_A_CHUNK + nbuf * kc * DTC_B_CHUNK + B * DTC_M * 4 +
+  return 1024 + stages * sc * DTC_A_CHUNK + nbuf * kc * DTC_B_CHUNK + B * DTC_M * 4 +
          ((n * 4 + 127) / 128) * 128 + (2 * stages + 2 * nbuf + 2 * DTC_ND + 1) * 8 + 16 +
          CTRL_INTS * 4 + route_smem_bytes(n, E, true);
 }
@@ -98,7 +102,9 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int I = a.I;
   const int kc = down_tc_kc(I);
   const int n = a.B * a.K;
-  const int SB = kc * DTC_A_CHUNK;  // bytes of one weight stage
+  const int SC = a.sc;              // K chunks per weight stage
+  const int nst = (kc + SC - 1) / SC;  // weight stages per item
+  const int SB = SC * DTC_A_CHUNK;  // bytes of one weight stage
   const int BB = kc * DTC_B_CHUNK;  // bytes of one h buffer
   uint8_t* wring = base;
   uint8_t* bring = wring + (size_t)S * SB;
@@ -183,22 +189,25 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
     bool ok = true;
-    for (int g = g_first; g < nsg; g = next_item(g)) {
-      const int slot = (int)(it % (uint32_t)S);
-      if (lane == 0) {
-        if (!wait(&wempty[slot], ((it / (uint32_t)S) & 1u) ^ 1u)) {
-          ok = false;
-        } else {
-          uint8_t* st = wring + (size_t)slot * SB;
-          mbar_arrive_expect_tx(&wfull[slot], (uint32_t)SB);
-          for (int c = 0; c < kc; ++c)
-            tma_load_3d(st + c * DTC_A_CHUNK, &tm_w, c * DTC_BK, j0, r.sg_exp[g], &wfull[slot],
-                        pol);
+    for (int g = g_first; ok && g < nsg; g = next_item(g)) {
+      for (int sj = 0; sj < nst; ++sj) {
+        const int slot = (int)(it % (uint32_t)S);
+        const int c0 = sj * SC, nc = min(SC, kc - c0);
+        if (lane == 0) {
+          if (!wait(&wempty[slot], ((it / (uint32_t)S) & 1u) ^ 1u)) {
+            ok = false;
+          } else {
+            uint8_t* st = wring + (size_t)slot * SB;
+            mbar_arrive_expect_tx(&wfull[slot], (uint32_t)(nc * DTC_A_CHUNK));
+            for (int c = 0; c < nc; ++c)
+              tma_load_3d(st + c * DTC_A_CHUNK, &tm_w, (c0 + c) * DTC_BK, j0, r.sg_exp[g],
+                          &wfull[slot], pol);
+          }
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++it;
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      ++it;
     }
     if (!ok && lane == 0) {
       const uint32_t lo = it > (uint32_t)S ? it - (uint32_t)S : 0u;
@@ -212,32 +221,38 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t it = 0;
-      bool issued = false;
+      uint32_t it = 0, its = 0;  // items, weight stages
+      bool issued = false, ok = true;
       const uint32_t idesc = tc_idesc_bf16(DTC_M, DTC_N);
-      for (int g = g_first; g < nsg; g = next_item(g)) {
-        const int slot = (int)(it % (uint32_t)S);
+      for (int g = g_first; ok && g < nsg; g = next_item(g)) {
         const int bb = (int)(it % (uint32_t)NB);
         const int d = (int)(it % (uint32_t)DTC_ND);
-        if (!wait(&wfull[slot], (it / (uint32_t)S) & 1u) ||
-            !wait(&bfull[bb], (it / (uint32_t)NB) & 1u) ||
+        if (!wait(&bfull[bb], (it / (uint32_t)NB) & 1u) ||
             !wait(&dempty[d], ((it / (uint32_t)DTC_ND) & 1u) ^ 1u))
           break;
         tc_fence_after();
-        const uint8_t* W = wring + (size_t)slot * SB;
         const uint8_t* Bt = bring + (size_t)bb * BB;
         const uint32_t dt = tmem + (uint32_t)(d * DTC_N);
-        for (int c = 0; c < kc; ++c) {
-          const uint64_t ad = tc_desc_sw128(smem_u32(W + c * DTC_A_CHUNK));
-          const uint64_t bd = tc_desc_sw128(smem_u32(Bt + c * DTC_B_CHUNK));
+        for (int sj = 0; sj < nst; ++sj, ++its) {
+          const int slot = (int)(its % (uint32_t)S);
+          if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u)) { ok = false; break; }
+          tc_fence_after();
+          const uint8_t* W = wring + (size_t)slot * SB;
+          const int c0 = sj * SC, nc = min(SC, kc - c0);
+          for (int cc = 0; cc < nc; ++cc) {
+            const int c = c0 + cc;
+            const uint64_t ad = tc_desc_sw128(smem_u32(W + cc * DTC_A_CHUNK));
+            const uint64_t bd = tc_desc_sw128(smem_u32(Bt + c * DTC_B_CHUNK));
 #pragma unroll
-          for (int kk = 0; kk < DTC_BK / 16; ++kk)
-            tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < DTC_BK / 16; ++kk)
+              tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&wempty[slot]);
+          issued = true;
         }
-        tc_commit(&wempty[slot]);
+        if (!ok) break;
         tc_commit(&bempty[bb]);
         tc_commit(&dfull[d]);
-        issued = true;
         ++it;
       }
       if (issued) {

@@ -389,12 +389,23 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_down) encode failed");
   const int n = bn * topk;
   const int budget = dev->smem_optin - 2048;
-  int stages = 4, nbuf = 8;
-  auto need = [&]() { return wdb::down_tc_smem_bytes(stages, nbuf, inter, bn, n, E); };
-  while (need() > budget && nbuf > wdb::DTC_GW) nbuf -= 2;
-  while (need() > budget && stages > 2) --stages;
-  if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
-  const int smem = need();
+  // Weight ring: as many K chunks in flight as fit (stages x chunks per
+  // stage), never fewer h buffers than gather warps.
+  const int kc = wdb::down_tc_kc(inter);
+  int stages = 0, sc = 0, nbuf = 0, smem = 0;
+  for (int c : {wdb::DTC_SC, 2, 1}) {
+    const int scc = std::min(c, kc);
+    for (int st = 4; st >= 2 && !smem; --st)
+      for (int nb : {8, 6, wdb::DTC_GW}) {
+        const int need = wdb::down_tc_smem_bytes(st, scc, nb, inter, bn, n, E);
+        if (need <= budget) {
+          stages = st; sc = scc; nbuf = nb; smem = need;
+          break;
+        }
+      }
+    if (smem) break;
+  }
+  if (!smem) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
   const int cl = down_tc_cluster(dev, hidden, smem);
   if (cl == 0) return fail(WD_ERR_UNSUPPORTED, "no cluster configuration fits");
   wdb::DownTcArgs a;
@@ -406,6 +417,7 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   a.status = status;
   a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
   a.stages = stages;
+  a.sc = sc;
   a.nbuf = nbuf;
   a.cl = cl;
   a.tp = {};
@@ -701,7 +713,7 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
   if ((rc = device_info(&dev))) return rc;
   if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK ||
       (hidden + wdb::DTC_M - 1) / wdb::DTC_M > dev->sm_count)
-    return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 256)");
+    return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 1024)");
   wdb::TpArgs tp = {};
   tp.world = c->world;
   tp.rank = c->rank;
