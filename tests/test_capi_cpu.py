@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 14, names
+    assert len(names) == 16, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -34,6 +34,24 @@ def test_gate_up_path_selector_validates():
     assert L.wd_set_down_path(-1) == capi.WD_ERR_SHAPE
     for p in (capi.PATH_SIMT, capi.PATH_TC, capi.PATH_AUTO):
         assert L.wd_set_down_path(p) == capi.WD_OK
+    assert L.wd_set_ffn_path(3) == capi.WD_ERR_SHAPE
+    for p in (capi.FFN_SPLIT, capi.FFN_FUSED, capi.FFN_AUTO):
+        assert L.wd_set_ffn_path(p) == capi.WD_OK
+
+
+def test_ffn_validates_before_touching_the_device():
+    L = capi.lib()
+    # shape / pointer / alignment errors come back before any CUDA call
+    assert capi.ffn(1, 1, 1, 1, 1, 1, None, 1, 0, 1, 128, 8, 4095, 192) == capi.WD_ERR_SHAPE
+    assert capi.ffn(16, 16, 16, 16, 16, None, None, 16, 0, 1, 128, 8, 4096, 192) == \
+        capi.WD_ERR_NULL_POINTER
+    assert capi.ffn(16, 16, 24, 16, 16, 16, None, 16, 0, 1, 128, 8, 4096, 192) == \
+        capi.WD_ERR_ALIGNMENT
+    assert capi.ffn(16, 16, 16, 16, 16, 16, 12, 16, 0, 1, 128, 8, 4096, 192) == \
+        capi.WD_ERR_ALIGNMENT
+    assert b"sync" in L.wd_last_error_message()
+    assert capi.ffn(None, None, None, None, None, None, None, None, 0, 0, 128, 8, 4096, 192) == \
+        capi.WD_OK
 
 
 def test_tp_comm_validates_before_touching_the_device():

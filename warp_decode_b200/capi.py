@@ -43,6 +43,9 @@ _SIGS = {
     "wd_tp_comm_destroy": (_I, [_P]),
     "wd_moe_down_3d_batched_allreduce": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
                                               _P]),
+    "wd_moe_ffn_3d_batched": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
+                                   _P]),
+    "wd_set_ffn_path": (_I, [_I]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -50,6 +53,8 @@ IPC_HANDLE_BYTES = 64
 # Values of wd_set_gate_up_path / wd_set_down_path.
 GATE_UP_AUTO, GATE_UP_SIMT, GATE_UP_TC = 0, 1, 2
 PATH_AUTO, PATH_SIMT, PATH_TC = 0, 1, 2
+# Values of wd_set_ffn_path.
+FFN_AUTO, FFN_SPLIT, FFN_FUSED = 0, 1, 2
 
 _lib = None
 
@@ -105,6 +110,17 @@ def down_mxfp8(h, wq, ws, ids, scale, out, out_fp32, B, E, topk, hidden, inter, 
                stream=0) -> int:
     return lib().wd_moe_down_3d_batched_mxfp8(h, wq, ws, ids, scale, out, out_fp32, B, E, topk,
                                               hidden, inter, status, stream)
+
+
+def ffn(x, w_gu, w_dn, ids, scale, h, sync, out, out_fp32, B, E, topk, hidden, inter,
+        status=None, stream=0) -> int:
+    return lib().wd_moe_ffn_3d_batched(x, w_gu, w_dn, ids, scale, h, sync, out, out_fp32, B, E,
+                                       topk, hidden, inter, status, stream)
+
+
+def set_ffn_path(path: int) -> None:
+    """Select the kernels behind wd_moe_ffn_3d_batched (FFN_AUTO / _SPLIT / _FUSED)."""
+    check(lib().wd_set_ffn_path(int(path)))
 
 
 def set_gate_up_path(path: int) -> None:

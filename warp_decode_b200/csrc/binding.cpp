@@ -172,6 +172,31 @@ torch::Tensor moe_down_3d_batched_mxfp8(torch::Tensor buffer, torch::Tensor w_q,
   return down_common(buffer, w_q, w_scale, topk_ids, topk_scale, B, fp32_out);
 }
 
+// gate_up -> down in one call (wd_moe_ffn_3d_batched; single launch for
+// B*topk <= 64).  Uses the library's grid-barrier words of the device: calls
+// on different streams of one device must not overlap.
+torch::Tensor moe_ffn_3d_batched(torch::Tensor x, torch::Tensor w_gate_up, torch::Tensor w_down,
+                                 torch::Tensor topk_ids, torch::Tensor topk_scale, bool fp32_out) {
+  const GateUpShape s = gate_up_shape(x, w_gate_up, topk_ids, false);
+  CHECK_CUDA(w_down); CHECK_CONTIG(w_down); CHECK_BF16(w_down);
+  CHECK_CUDA(topk_scale); CHECK_CONTIG(topk_scale); CHECK_F32(topk_scale);
+  check_same_device(x, w_down, "w_down");
+  check_same_device(x, topk_scale, "topk_scale");
+  TORCH_CHECK(w_down.dim() == 3 && w_down.size(0) == s.E && w_down.size(1) == s.hidden &&
+                  w_down.size(2) == s.inter,
+              "w_down must be [E, hidden, inter]");
+  TORCH_CHECK(topk_scale.dim() == 2 && topk_scale.size(0) == s.B && topk_scale.size(1) == s.topk,
+              "topk_scale must be [B, topk]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto h = torch::empty({(int64_t)s.B * s.topk, s.inter}, x.options().dtype(at::kBFloat16));
+  auto out = torch::empty({s.B, s.hidden}, x.options().dtype(fp32_out ? at::kFloat : at::kBFloat16));
+  check_rc(wd_moe_ffn_3d_batched(x.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(),
+                                 topk_ids.data_ptr<int32_t>(), topk_scale.data_ptr<float>(),
+                                 h.data_ptr(), nullptr, out.data_ptr(), fp32_out ? 1 : 0, s.B, s.E,
+                                 s.topk, s.hidden, s.inter, nullptr, stream_ptr()));
+  return out;
+}
+
 int64_t status(bool clear, int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   uint32_t v = 0;
@@ -181,6 +206,7 @@ int64_t status(bool clear, int64_t device) {
 
 void set_gate_up_path(int64_t path) { check_rc(wd_set_gate_up_path(static_cast<int>(path))); }
 void set_down_path(int64_t path) { check_rc(wd_set_down_path(static_cast<int>(path))); }
+void set_ffn_path(int64_t path) { check_rc(wd_set_ffn_path(static_cast<int>(path))); }
 
 }  // namespace
 
@@ -202,6 +228,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Fused MoE down + top-k weighted sum with MXFP8 weights", py::arg("buffer"),
         py::arg("w_q"), py::arg("w_scale"), py::arg("topk_ids"), py::arg("topk_scale"),
         py::arg("B") = py::none(), py::arg("fp32_out") = false);
+  m.def("moe_ffn_3d_batched", &moe_ffn_3d_batched,
+        "gate_up + silu*up + down + top-k weighted sum in one call (one launch for B*topk <= 64)",
+        py::arg("x"), py::arg("w_gate_up"), py::arg("w_down"), py::arg("topk_ids"),
+        py::arg("topk_scale"), py::arg("fp32_out") = false);
   m.def("status", &status, "Read (and clear) the device status word of the library",
         py::arg("clear") = true, py::arg("device") = 0);
   m.def("set_gate_up_path", &set_gate_up_path,
@@ -209,5 +239,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("path"));
   m.def("set_down_path", &set_down_path,
         "down kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
+        py::arg("path"));
+  m.def("set_ffn_path", &set_ffn_path,
+        "moe_ffn_3d_batched kernels for later calls: 0 automatic, 1 two launches, 2 one launch",
         py::arg("path"));
 }

@@ -262,9 +262,10 @@ struct NoInit {
 // Routing of one launch, computed by every CTA (all threads; ends with
 // __syncthreads).  Validates topk_ids (out-of-range ids become -1 and raise
 // WD_STATUS_BAD_EXPERT_ID), then groups the slots by expert:
-//  * dedup: one group per touched expert, in ascending expert id, members
+//  * dedup: one group per touched expert (for n <= 64 in the order of first
+//    appearance, found by one warp; else in ascending expert id), members
 //    in slot order, split into groups of at most `cap` members; all invalid
-//    slots form the last group(s) with expert -1.  A stable counting sort:
+//    slots form one group with expert -1.  For n > 64 a stable counting sort:
 //    with at most 64 tokens and no expert repeated inside a token, each
 //    expert's 64-bit token mask (shared-memory atomicOr) gives every slot
 //    its rank directly; otherwise one warp ranks the slots 32 at a time
@@ -322,6 +323,75 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
       r.mtok[i] = i / K;
     }
     if (tid == 0) *r.nsg = n;
+    __syncthreads();
+    return;
+  }
+  if (n <= 64) {
+    // Small launch: one warp groups all slots (first-appearance order of
+    // the experts, members in slot order) with shared-memory atomics on the
+    // touched buckets only and ballot/shuffle scans: one block barrier.
+    if (warp == 0) {
+      int* first = reinterpret_cast<int*>(r.mask);  // [E+1] first slot of each bucket
+      int* c0 = r.cnt;                              // [E+1] slots in 0..31
+      int* c1 = r.off;                              // [E+1] slots in 32..63
+      const int i0 = lane, i1 = lane + 32;
+      const bool v0 = i0 < n, v1 = i1 < n;
+      const int k0 = v0 ? (r.ids[i0] < 0 ? E : r.ids[i0]) : -1;
+      const int k1 = v1 ? (r.ids[i1] < 0 ? E : r.ids[i1]) : -1;
+      if (v0) { first[k0] = 0x7fffffff; c0[k0] = 0; c1[k0] = 0; }
+      if (v1) { first[k1] = 0x7fffffff; c0[k1] = 0; c1[k1] = 0; }
+      __syncwarp();
+      if (v0) { atomicMin(&first[k0], i0); atomicAdd(&c0[k0], 1); }
+      if (v1) { atomicMin(&first[k1], i1); atomicAdd(&c1[k1], 1); }
+      __syncwarp();
+      const unsigned lt = (1u << lane) - 1u;
+      const unsigned m0 = __match_any_sync(0xffffffffu, v0 ? k0 : -2 - lane);
+      const unsigned m1 = __match_any_sync(0xffffffffu, v1 ? k1 : -2 - lane);
+      const int rank0 = __popc(m0 & lt);
+      const int rank1 = (v1 ? c0[k1] : 0) + __popc(m1 & lt);
+      const bool f0 = v0 && first[k0] == i0, f1 = v1 && first[k1] == i1;
+      const int sz0 = f0 ? c0[k0] + c1[k0] : 0, sz1 = f1 ? c0[k1] + c1[k1] : 0;
+      const int ns0 = (sz0 + cap - 1) / cap, ns1 = (sz1 + cap - 1) / cap;
+      // Exclusive scans in group (= slot) order of sizes and subgroup counts.
+      int a0 = sz0, a1 = sz1, s0 = ns0, s1 = ns1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t0 = __shfl_up_sync(0xffffffffu, a0, o), t1 = __shfl_up_sync(0xffffffffu, a1, o);
+        const int u0 = __shfl_up_sync(0xffffffffu, s0, o), u1 = __shfl_up_sync(0xffffffffu, s1, o);
+        if (lane >= o) { a0 += t0; a1 += t1; s0 += u0; s1 += u1; }
+      }
+      const int tot_a0 = __shfl_sync(0xffffffffu, a0, 31), tot_s0 = __shfl_sync(0xffffffffu, s0, 31);
+      const int off0 = a0 - sz0, off1 = tot_a0 + a1 - sz1;      // member offset of the group
+      const int so0 = s0 - ns0, so1 = tot_s0 + s1 - ns1;        // first subgroup of the group
+      if (lane == 31) *r.nsg = tot_s0 + s1;
+      if (f0)
+        for (int j = 0; j < ns0; ++j) {
+          r.sg_exp[so0 + j] = k0 < E ? k0 : -1;
+          r.sg_beg[so0 + j] = off0 + j * cap;
+          r.sg_cnt[so0 + j] = min(cap, sz0 - j * cap);
+        }
+      if (f1)
+        for (int j = 0; j < ns1; ++j) {
+          r.sg_exp[so1 + j] = k1 < E ? k1 : -1;
+          r.sg_beg[so1 + j] = off1 + j * cap;
+          r.sg_cnt[so1 + j] = min(cap, sz1 - j * cap);
+        }
+      // Member position = offset of the slot's group + its rank: the group's
+      // offset lives in the lane of the group's first slot.
+      const int fs0 = v0 ? first[k0] : 0, fs1 = v1 ? first[k1] : 0;
+      const int o00 = __shfl_sync(0xffffffffu, off0, fs0 & 31), o01 = __shfl_sync(0xffffffffu, off1, fs0 & 31);
+      const int o10 = __shfl_sync(0xffffffffu, off0, fs1 & 31), o11 = __shfl_sync(0xffffffffu, off1, fs1 & 31);
+      if (v0) {
+        const int p = (fs0 < 32 ? o00 : o01) + rank0;
+        r.members[p] = i0;
+        r.mtok[p] = i0 / K;
+      }
+      if (v1) {
+        const int p = (fs1 < 32 ? o10 : o11) + rank1;
+        r.members[p] = i1;
+        r.mtok[p] = i1 / K;
+      }
+    }
     __syncthreads();
     return;
   }

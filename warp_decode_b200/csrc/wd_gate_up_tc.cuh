@@ -48,6 +48,7 @@ struct GateUpTcArgs {
   int stages;           // smem ring depth
   int npad;             // MMA N: B rounded up to 16 (<= TC_NMAX)
   int kch;              // 64-wide K chunks per stage
+  int cl;               // CTAs per cluster: each takes 1/cl of K of every item
 };
 
 constexpr int TC_XCH = 8;                     // members per epilogue exchange round
@@ -57,9 +58,15 @@ __host__ __device__ inline int gate_up_tc_stage_bytes(int kch, int npad) {
   return kch * (TC_A_BYTES + npad * TC_BK * 2);
 }
 
-__host__ inline int gate_up_tc_smem_bytes(int stages, int kch, int npad, int n, int E) {
+// Split-K partials of one exchange round: [2][cl - 1][TC_XCH members][128 rows].
+__host__ __device__ inline int gate_up_tc_xbuf_bytes(int cl) {
+  return 2 * (cl - 1) * TC_XCH * TC_M * 4;
+}
+
+__host__ inline int gate_up_tc_smem_bytes(int stages, int kch, int npad, int n, int E, int cl) {
   return 1024 + stages * gate_up_tc_stage_bytes(kch, npad) + TC_XCH * TC_NEUR * 4 +
-         (2 * stages + 5) * 8 + 16 + CTRL_INTS * 4 + route_smem_bytes(n, E, true);
+         gate_up_tc_xbuf_bytes(cl) + (2 * stages + 9) * 8 + 16 + CTRL_INTS * 4 +
+         route_smem_bytes(n, E, true);
 }
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -74,14 +81,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int KCH = a.kch;
   const int BT = a.npad * TC_BK * 2;  // bytes of one B chunk
   const int SB = gate_up_tc_stage_bytes(KCH, a.npad);
+  const int CL = a.cl;
   uint8_t* ring = base;
   float* xch = reinterpret_cast<float*>(ring + (size_t)S * SB);  // [TC_XCH][64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(xch + TC_XCH * TC_NEUR);
+  float* xbuf = xch + TC_XCH * TC_NEUR;  // [2][CL-1][TC_XCH][128] (cluster rank 0)
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) +
+                                               gate_up_tc_xbuf_bytes(CL));
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;   // [2] accumulator ready
   uint64_t* tempty = tfull + 2;  // [2] accumulator drained
   uint64_t* done = tempty + 2;   // MMA drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* xfull = done + 1;    // [2] rank 0: partials of a round arrived
+  uint64_t* xempty = xfull + 2;  // [2] ranks > 0: rank 0 consumed a round's slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + 2);
   volatile int* ctrl = reinterpret_cast<volatile int*>(tmem_slot + 4);
   int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
 
@@ -102,6 +114,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[0], 4);
       mbar_init(&tempty[1], 4);
       mbar_init(done, 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&xfull[b], (uint32_t)max(1, CL - 1) * 128u);
+        mbar_init(&xempty[b], 128u);
+      }
       ctrl[0] = 0;
       fence_mbar_init();
     }
@@ -121,9 +137,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int n_tiles = (a.I + TC_NEUR - 1) / TC_NEUR;
   const int items = *r.nsg * n_tiles;
-  const int nkc = (a.H + TC_BK - 1) / TC_BK;  // 64-wide K chunks
+  const int nkc_all = (a.H + TC_BK - 1) / TC_BK;  // 64-wide K chunks of a row
+  // Cluster rank `crank` of cluster `cid` covers chunks [kc_lo, kc_lo + nkc)
+  // of every item of its cluster; rank 0 sums the partials and stores h.
+  const int crank = CL > 1 ? (int)cluster_ctarank() : 0;
+  const int kc_lo = crank * nkc_all / CL;
+  const int nkc = (crank + 1) * nkc_all / CL - kc_lo;
   const int nk = (nkc + KCH - 1) / KCH;        // stages per item
-  const int G = (int)gridDim.x;
+  const int G = (int)gridDim.x / CL;           // clusters
+  const int cid = (int)blockIdx.x / CL;
 
   // Bounded wait that also gives up once another role has aborted.
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -148,7 +170,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint64_t pol_x = l2_policy_evict_last();
     uint32_t it = 0;
     bool ok = true;
-    for (int t = (int)blockIdx.x; ok && t < items; t += G) {
+    for (int t = cid; ok && t < items; t += G) {
       const int g = t / n_tiles, mt = t - g * n_tiles;
       const int e = r.sg_exp[g];
       if (e < 0) continue;
@@ -159,7 +181,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (!wait(&empty[slot], ph ^ 1u)) {
             ok = false;
           } else {
-            const int c0 = ks * KCH, nc = min(KCH, nkc - c0);
+            const int c0 = kc_lo + ks * KCH, nc = min(KCH, kc_lo + nkc - c0);
             uint8_t* st = ring + (size_t)slot * SB;
             mbar_arrive_expect_tx(&full[slot], (uint32_t)nc * (TC_A_BYTES + BT));
             for (int c = 0; c < nc; ++c)
@@ -191,7 +213,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t it = 0, vi = 0;
       bool ok = true;
       bool issued = false;
-      for (int t = (int)blockIdx.x; ok && t < items; t += G) {
+      for (int t = cid; ok && t < items; t += G) {
         const int g = t / n_tiles;
         if (r.sg_exp[g] < 0) continue;
         const uint32_t buf = vi & 1u;
@@ -231,19 +253,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ---------------- epilogue: warps 2..5, TMEM lane quarter warp % 4 -----
     // Quarters 0, 1 read gate rows (neurons 32q + lane), quarters 2, 3 the
-    // up rows of the same neurons; up values cross over in `xch`.
+    // up rows of the same neurons; up values cross over in `xch`.  With
+    // clusters (CL > 1) ranks > 0 push their FP32 partials of each round of
+    // TC_XCH members into rank 0's `xbuf` over distributed shared memory;
+    // rank 0 adds them in rank order and alone stores h.
     const int q = warp & 3;
     const bool is_gate = q < 2;
     const int I = a.I;
-    uint32_t vi = 0;
-    for (int t = (int)blockIdx.x; t < items; t += G) {
+    const int row = 32 * q + lane;  // TMEM lane = A row
+    uint32_t vi = 0, rr = 0;        // valid items, exchange rounds
+    auto waitc = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 31u) == 31u && ctrl[0]) return false;
+        if ((it & 31u) == 31u && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+          raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+          ctrl[0] = 1;
+          return false;
+        }
+      }
+    };
+    for (int t = cid; t < items; t += G) {
       const int g = t / n_tiles, mt = t - g * n_tiles;
       const int e = r.sg_exp[g];
       const int cnt = r.sg_cnt[g], beg = r.sg_beg[g];
       const int nn = mt * TC_NEUR + 32 * (q & 1) + lane;
       if (e < 0) {
         // A slot with an out-of-range expert id yields zeros.
-        if (is_gate && nn < I)
+        if (crank == 0 && is_gate && nn < I)
           for (int c = 0; c < cnt; ++c)
             a.out[(size_t)r.members[beg + c] * I + nn] = __float2bfloat16_rn(0.f);
         continue;
@@ -251,22 +289,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t buf = vi & 1u;
       // A failed (timed-out) wait still runs the exchange rounds so the four
       // warps meet at every bar.sync; nothing is stored from such an item.
-      const bool got = wait(&tfull[buf], (vi >> 1) & 1u);
+      bool got = wait(&tfull[buf], (vi >> 1) & 1u);
       __syncwarp();  // tcgen05.ld and bar.sync below are warp-collective
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + buf * TC_NMAX;
-      for (int c0 = 0; c0 < cnt; c0 += TC_XCH) {
+      for (int c0 = 0; c0 < cnt; c0 += TC_XCH, ++rr) {
         // Column of member c = its token; members past cnt re-read column 0.
-        uint32_t v[TC_XCH];
+        float v[TC_XCH];
 #pragma unroll
         for (int j = 0; j < TC_XCH; ++j) {
           const int tok = c0 + j < cnt ? r.mtok[beg + c0 + j] : 0;
-          v[j] = tmem_ld_x1(taddr + (uint32_t)tok);
+          v[j] = __uint_as_float(tmem_ld_x1(taddr + (uint32_t)tok));
         }
         tmem_wait_ld();
+        if (CL > 1) {
+          const uint32_t xb = rr & 1u, xpar = (rr >> 1) & 1u;
+          float* slot0 = xbuf + (size_t)xb * (CL - 1) * TC_XCH * TC_M;
+          if (crank > 0) {
+            // Wait until rank 0 has consumed this slot's previous round, push
+            // this rank's partials, signal rank 0.
+            got = waitc(&xempty[xb], xpar ^ 1u) && got;
+            float* dst = slot0 + (size_t)(crank - 1) * TC_XCH * TC_M + row;
+#pragma unroll
+            for (int j = 0; j < TC_XCH; ++j) dsmem_st_f32(dsmem_addr(dst + j * TC_M, 0), v[j]);
+            mbar_arrive_remote(dsmem_addr(&xfull[xb], 0));
+            continue;  // ranks > 0 store nothing
+          }
+          got = waitc(&xfull[xb], xpar) && got;
+          for (int k = 1; k < CL; ++k) {
+            const float* src = slot0 + (size_t)(k - 1) * TC_XCH * TC_M + row;
+#pragma unroll
+            for (int j = 0; j < TC_XCH; ++j) v[j] += src[j * TC_M];
+          }
+          for (int k = 1; k < CL; ++k) mbar_arrive_remote(dsmem_addr(&xempty[xb], (uint32_t)k));
+        }
         if (!is_gate) {
 #pragma unroll
-          for (int j = 0; j < TC_XCH; ++j) xch[j * TC_NEUR + 32 * (q & 1) + lane] = __uint_as_float(v[j]);
+          for (int j = 0; j < TC_XCH; ++j) xch[j * TC_NEUR + 32 * (q & 1) + lane] = v[j];
         }
         named_barrier_sync(1, 128);
         if (is_gate && got && nn < I) {
@@ -275,7 +334,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (c0 + j < cnt) {
               const float u = xch[j * TC_NEUR + 32 * q + lane];
               a.out[(size_t)r.members[beg + c0 + j] * I + nn] =
-                  __float2bfloat16_rn(silu_f32(__uint_as_float(v[j])) * u);
+                  __float2bfloat16_rn(silu_f32(v[j]) * u);
             }
           }
         }
@@ -294,6 +353,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);
   }
+  // No CTA leaves while a peer may still write into its shared memory.
+  if (CL > 1) cluster_sync();
 }
 
 }  // namespace wdb

@@ -18,12 +18,14 @@
 
 #include <array>
 #include <atomic>
+#include <cmath>
 #include <vector>
 
 #include "wd_down.cuh"
 #include "wd_gate_up.cuh"
 #include "wd_gate_up_tc.cuh"
 #include "wd_down_tc.cuh"
+#include "wd_ffn.cuh"
 
 namespace {
 
@@ -39,6 +41,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sm_count = 0;
   int smem_optin = 0;
+  uint32_t* ffn_sync = nullptr;  // library-owned grid-barrier words (g_wd_ffn_sync)
   bool ready = false;
 };
 
@@ -65,6 +68,7 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_kernel),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -78,6 +82,8 @@ int device_info(DeviceInfo** out) {
         err = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
                                    (int)cudaSharedmemCarveoutMaxShared);
     }
+    if (err == cudaSuccess)
+      err = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.ffn_sync), wdb::g_wd_ffn_sync);
     if (err != cudaSuccess)
       return fail(WD_ERR_CUDA, std::string("device setup: ") + cudaGetErrorString(err));
     d.ready = true;
@@ -146,6 +152,24 @@ int kernel_path(std::atomic<int>& slot, const char* env) {
 int gate_up_path() { return kernel_path(g_gate_up_path, "WARP_DECODE_GATE_UP"); }
 int down_path() { return kernel_path(g_down_path, "WARP_DECODE_DOWN"); }
 
+// FFN entry point: 0 = automatic (single-launch kernel wherever it applies),
+// 1 = always the two kernels, 2 = single launch wherever it applies.
+// WARP_DECODE_FFN=split|fused sets the initial choice.
+std::atomic<int> g_ffn_path{-1};
+int ffn_path() {
+  int p = g_ffn_path.load(std::memory_order_relaxed);
+  if (p < 0) {
+    const char* v = std::getenv("WARP_DECODE_FFN");
+    p = 0;
+    if (v && std::strcmp(v, "split") == 0) p = 1;
+    if (v && std::strcmp(v, "fused") == 0) p = 2;
+    int expected = -1;
+    g_ffn_path.compare_exchange_strong(expected, p);
+    p = g_ffn_path.load(std::memory_order_relaxed);
+  }
+  return p;
+}
+
 // cuTensorMapEncodeTiled from the driver, resolved once through the runtime.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -163,6 +187,44 @@ EncodeTiledFn encode_tiled() {
     return reinterpret_cast<EncodeTiledFn>(p);
   }();
   return fn;
+}
+
+#ifndef WD_TC_MAX_CLUSTER
+#define WD_TC_MAX_CLUSTER 8
+#endif
+
+// How many clusters of `cl` gate_up CTAs with `smem` bytes each can be
+// resident at once (occupancy calculator; cached per device and shape).
+int gate_up_tc_active_clusters(int cl, int smem) {
+  static std::mutex mu;
+  static std::vector<std::array<int, 4>> cache;  // {device, cl, smem, clusters}
+  int devno = 0;
+  cudaGetDevice(&devno);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& c : cache)
+      if (c[0] == devno && c[1] == cl && c[2] == smem) return c[3];
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cl);
+  cfg.blockDim = dim3(wdb::TC_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int nc = 0;
+  if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_gate_up_tc_kernel, &cfg) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    nc = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({devno, cl, smem, nc});
+  return nc;
 }
 
 // Tensor-core gate_up for one launch chunk of bn tokens.
@@ -197,9 +259,34 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
   // Stages of WD_TC_KCH 64-wide K chunks (each weight row is then read in
   // WD_TC_KCH * 128 contiguous bytes), as many as fit, at most 8.
   const int kch = WD_TC_KCH;
-  int stages = 8;
-  while (stages > 2 && wdb::gate_up_tc_smem_bytes(stages, kch, npad, n, E) > budget) --stages;
-  const int smem = wdb::gate_up_tc_smem_bytes(stages, kch, npad, n, E);
+  auto plan = [&](int cl, int* stages_out) {
+    int st = 8;
+    while (st > 2 && wdb::gate_up_tc_smem_bytes(st, kch, npad, n, E, cl) > budget) --st;
+    *stages_out = st;
+    return wdb::gate_up_tc_smem_bytes(st, kch, npad, n, E, cl);
+  };
+  // Few items (small B): split K over a cluster of cl CTAs, so that the
+  // busiest CTA streams ceil(items / clusters) / cl items' worth of weights
+  // instead of whole items on a fraction of the SMs.  Items are estimated
+  // from the expected number of distinct experts under uniform routing.
+  const int n_tiles = (inter + wdb::TC_NEUR - 1) / wdb::TC_NEUR;
+  const double u_est =
+      E * (1.0 - std::pow(1.0 - std::min(topk, E) / (double)E, (double)bn));
+  const int items_est = std::max(1, (int)std::ceil(u_est)) * n_tiles;
+  int cl = 1, stages = 0, ncl = 0;
+  int smem = plan(1, &stages);
+  double best = 1e30;
+  const int nkc_all = (hidden + wdb::TC_BK - 1) / wdb::TC_BK;
+  for (int c = 1; c <= std::min(WD_TC_MAX_CLUSTER, nkc_all); ++c) {  // >= 1 K chunk per CTA
+    int st = 0;
+    const int sm = plan(c, &st);
+    if (sm > budget) continue;
+    int nc = dev->sm_count / c;
+    if (c > 1) nc = std::min(nc, gate_up_tc_active_clusters(c, sm));
+    if (nc < 1) continue;
+    const double cost = std::ceil((double)items_est / nc) / c + 0.02 * (c - 1);
+    if (cost < best) { best = cost; cl = c; stages = st; smem = sm; ncl = nc; }
+  }
   if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
   wdb::GateUpTcArgs a;
   a.ids = ids;
@@ -209,9 +296,21 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
   a.stages = stages;
   a.npad = npad;
   a.kch = kch;
-  const long long work = (long long)n * ((inter + wdb::TC_NEUR - 1) / wdb::TC_NEUR);
+  a.cl = cl;
+  const long long work = (long long)n * n_tiles;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+  cudaLaunchAttribute attr[1];
+  if (cl > 1) {
+    cfg.gridDim = dim3((unsigned)(ncl * cl));
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  } else {
+    cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+  }
   cfg.blockDim = dim3(wdb::TC_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
@@ -551,6 +650,114 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
   return WD_OK;
 }
 
+// ---- single-launch FFN ------------------------------------------------------
+struct FfnPlan {
+  int depth = 0, kc = 0, rc = 0, lpr = 0, rows_max = 0, stage_bytes = 0, xh_bytes = 0;
+  int smem = 0, grid = 0;
+  bool dedup = false;
+};
+
+// Whether moe_ffn_kernel runs on this device with `smem` bytes of shared
+// memory at one CTA per SM (cooperative launch: all CTAs co-resident).
+bool ffn_fits(const DeviceInfo* dev, int smem) {
+  static std::mutex mu;
+  static std::vector<std::array<int, 3>> cache;  // {device, smem, fits}
+  int devno = 0;
+  cudaGetDevice(&devno);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& c : cache)
+      if (c[0] == devno && c[1] == smem) return c[2] != 0;
+  }
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, wdb::moe_ffn_kernel, wdb::FFN_THREADS,
+                                                    (size_t)smem) != cudaSuccess) {
+    cudaGetLastError();
+    nb = 0;
+  }
+  (void)dev;
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({devno, smem, nb >= 1 ? 1 : 0});
+  return nb >= 1;
+}
+
+// Launch geometry of the single-launch FFN, or false where it does not apply:
+// more than 64 routed slots, E above the dedup table, or x / h of the call
+// too large for shared memory next to a two-slot ring.
+bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int inter, FfnPlan* pl) {
+  const int n = B * topk;
+  if (n < 1 || n > wdb::FFN_MAX_SLOTS) return false;
+  if (hidden % 8 != 0 || inter % 8 != 0) return false;
+  const bool dedup = n > 1;
+  if (dedup && E > wdb::MAX_DEDUP_E) return false;
+  FfnPlan p;
+  p.grid = dev->sm_count;
+  p.rows_max = (hidden + p.grid - 1) / p.grid;
+  p.kc = 2048;  // bf16 elements: 4 KB gate and up row chunks
+  const int row_bytes = inter * 2;
+  p.stage_bytes = std::max(wdb::gate_up_stage_bytes(wdb::W_BF16, p.kc), ((row_bytes + 127) / 128) * 128);
+  // Down chunks: as many of the CTA's rows as fit a slot, split evenly.
+  const int rc_cap = std::max(1, p.stage_bytes / row_bytes);
+  const int nch = (p.rows_max + rc_cap - 1) / rc_cap;
+  p.rc = (p.rows_max + nch - 1) / nch;
+  const int nvec = inter / 8;
+  p.lpr = nvec <= 32 ? 8 : (nvec <= 64 ? 16 : 32);
+  p.xh_bytes = std::max(B * hidden * 2, n * inter * 2);
+  p.dedup = dedup;
+  const int budget = dev->smem_optin - 2048;
+  for (int depth : {4, 3, 2}) {
+    const int need = wdb::ffn_smem_bytes(depth, p.stage_bytes, p.xh_bytes, B, p.rows_max, n, E,
+                                         dedup);
+    if (need <= budget && ffn_fits(dev, need)) {
+      p.depth = depth;
+      p.smem = need;
+      *pl = p;
+      return true;
+    }
+  }
+  return false;
+}
+
+int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const void* w_gu,
+               const void* w_dn, const int32_t* ids, const float* scale, void* h, uint32_t* sync,
+               void* y, int out_fp32, int B, int E, int topk, int hidden, int inter,
+               uint32_t* status, cudaStream_t s) {
+  wdb::FfnArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  a.wgu = reinterpret_cast<const uint8_t*>(w_gu);
+  a.wdn = reinterpret_cast<const uint8_t*>(w_dn);
+  a.ids = ids;
+  a.scale = scale;
+  a.h = reinterpret_cast<__nv_bfloat16*>(h);
+  a.sync = sync;
+  a.out = y;
+  a.out_fp32 = out_fp32 ? 1 : 0;
+  a.status = status;
+  a.B = B; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+  a.dedup = p.dedup ? 1 : 0;
+  a.depth = p.depth;
+  a.stage_bytes = p.stage_bytes;
+  a.kc = p.kc;
+  a.rc = p.rc;
+  a.lpr = p.lpr;
+  a.rows_max = p.rows_max;
+  a.xh_bytes = p.xh_bytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.grid);
+  cfg.blockDim = dim3(wdb::FFN_THREADS);
+  cfg.dynamicSmemBytes = (size_t)p.smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel, a);
+  if (err != cudaSuccess)
+    return fail(WD_ERR_CUDA, std::string("ffn launch: ") + cudaGetErrorString(err));
+  return WD_OK;
+}
+
 // ---- tensor-parallel communicator for the fused all-reduce ------------------
 struct TpComm {
   int device = -1;
@@ -627,6 +834,45 @@ int wd_set_down_path(int path) {
   if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
   g_down_path.store(path);
   return WD_OK;
+}
+
+int wd_set_ffn_path(int path) {
+  g_last_error.clear();
+  if (path < 0 || path > 2)
+    return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (split) or 2 (fused)");
+  g_ffn_path.store(path);
+  return WD_OK;
+}
+
+int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_down,
+                          const int32_t* topk_ids, const float* topk_scale, void* h_buf,
+                          uint32_t* sync, void* y_out, int out_fp32, int B, int E, int topk,
+                          int hidden, int inter, uint32_t* status, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (hidden % 8 != 0 || inter % 8 != 0)
+    return fail(WD_ERR_SHAPE, "hidden and inter must be multiples of 8 (16-byte weight rows)");
+  if (B == 0) return WD_OK;
+  if (!x || !w_gate_up || !w_down || !topk_ids || !topk_scale || !h_buf || !y_out)
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down) || !aligned16(h_buf))
+    return fail(WD_ERR_ALIGNMENT, "x, w_gate_up, w_down and h_buf must be 16-byte aligned");
+  if (sync && (reinterpret_cast<uintptr_t>(sync) & 7u) != 0)
+    return fail(WD_ERR_ALIGNMENT, "sync must be 8-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  FfnPlan plan;
+  if (ffn_path() != 1 && ffn_plan(dev, B, E, topk, hidden, inter, &plan))
+    return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
+                      sync ? sync : dev->ffn_sync, y_out, out_fp32, B, E, topk, hidden, inter,
+                      status, reinterpret_cast<cudaStream_t>(stream));
+  rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
+                                 topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
+  if (rc) return rc;
+  return down_impl<wdb::W_BF16>(h_buf, reinterpret_cast<const uint8_t*>(w_down), nullptr,
+                                topk_ids, topk_scale, y_out, out_fp32, B, E, topk, hidden, inter,
+                                status, stream);
 }
 
 int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, void** comm,

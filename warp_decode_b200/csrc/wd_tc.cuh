@@ -162,10 +162,15 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                    "memory");
 }
-// The two halves of cluster_sync, for work in between.
+// The two halves of cluster_sync, for work in between.  Call after a
+// __syncthreads() that follows the CTA's shared-memory writes: one
+// cluster-scope fence by thread 0 releases them (cumulative over the CTA
+// barrier), every thread then arrives relaxed.  Measured on B200, an
+// `arrive.release` by every thread here took 3-5 us; this form 0.06 us.
 __device__ __forceinline__ void cluster_arrive() {
+  if (threadIdx.x == 0) asm volatile("fence.acq_rel.cluster;" ::: "memory");
   __syncwarp();
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   __syncwarp();
@@ -189,6 +194,26 @@ __device__ __forceinline__ float dsmem_ld_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
+}
+
+// mbarrier operations across the CTAs of a cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // 32 lanes x 16 consecutive 32-bit columns.
