@@ -161,19 +161,20 @@ WD_API int wd_set_down_path(int path);
  * above back to back: benchmark/bench.py:205,254-255):
  *   h_buf = moe_gate_up(x, w_gate_up, topk_ids)          [B*topk, inter] bf16
  *   y_out = moe_down(h_buf, w_down, topk_ids, topk_scale) [B, hidden] bf16 (fp32 if out_fp32)
- * Same arithmetic and tolerances as the two entry points.  With at most 64
- * routed slots (B*topk <= 64) and x, h of the call fitting in shared memory
- * (E <= 1024 when B*topk > 1) it is ONE cooperative launch of one CTA per SM:
- * the down weights stream while gate_up still computes, and a grid barrier
- * orders h.  Otherwise it runs the two kernels of wd_moe_gate_up_3d_batched and
- * wd_moe_down_3d_batched.  Requirements: hidden % 8 == 0, inter % 8 == 0, x,
+ * Same arithmetic and tolerances as the two entry points.  For small calls
+ * (automatic choice: B*topk <= 32; forced single launch: <= 64) with x, h of
+ * the call fitting in shared memory (E <= 1024 when B*topk > 1) it is ONE
+ * cooperative launch of one CTA per SM: the down weights stream while
+ * gate_up still computes, and a grid barrier orders h.  Otherwise it runs the
+ * two kernels of wd_moe_gate_up_3d_batched and wd_moe_down_3d_batched.  Requirements: hidden % 8 == 0, inter % 8 == 0, x,
  * the weights and h_buf 16-byte aligned.
- * sync: 2 uint32 words of device memory (8-byte aligned), zero before their
- * first use; every call leaves them ready for the next.  NULL selects words
- * owned by the library (one pair per device).  Calls that share sync words
- * must not run at the same time (issue them on one stream, or order them
- * with events); give each concurrently used stream its own pair.  After a
- * call that raised WD_STATUS_WAIT_TIMEOUT, zero the words again.
+ * sync: 8 bytes of device memory (8-byte aligned; a 64-bit grid-barrier
+ * counter), zero before their first use; each single-launch call adds one per
+ * CTA (the SM count) and needs nothing else reset.  The counter belongs to
+ * one device.  NULL selects a counter owned by the library (one per device).
+ * Calls that share a counter must not run at the same time (issue them on one
+ * stream, or order them with events); give each concurrently used stream its
+ * own.  After a call that raised WD_STATUS_WAIT_TIMEOUT, zero it again.
  * Call once per device before capturing it in a CUDA graph (one-time device
  * setup).
  */
@@ -184,8 +185,8 @@ WD_API int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const voi
 
 /*
  * Kernel choice behind wd_moe_ffn_3d_batched for later calls in this process:
- * 0 = automatic (single launch wherever it applies), 1 = always the two
- * kernels, 2 = single launch wherever it applies.  WARP_DECODE_FFN=split|fused
+ * 0 = automatic (single launch up to 32 routed slots), 1 = always the two
+ * kernels, 2 = single launch wherever it applies (up to 64 routed slots).  WARP_DECODE_FFN=split|fused
  * sets the initial choice.
  */
 WD_API int wd_set_ffn_path(int path);

@@ -107,9 +107,17 @@ def test_qwen3_tp8(wd, B):
     assert st == 0
     check(host_bits(y_split), y_ref, f"split y B={B}")
     # torch entry point = the same kernel
-    y_t = wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale)
-    torch.cuda.synchronize()
+    capi.set_ffn_path(capi.FFN_FUSED)
+    try:
+        y_t = wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale)
+        torch.cuda.synchronize()
+    finally:
+        capi.set_ffn_path(capi.FFN_AUTO)
     assert np.array_equal(host_bits(y_t), host_bits(y))
+    # automatic choice: single launch up to 32 routed slots, two kernels above
+    y_auto, _, st = run_ffn(capi.FFN_AUTO, x, wgu, wdn, ids, scale)
+    assert st == 0
+    assert np.array_equal(host_bits(y_auto), host_bits(y if B * c.topk <= 32 else y_split))
 
 
 # (B, hidden, inter, E, topk, routing): ragged rows per CTA, small and large
@@ -157,12 +165,13 @@ def test_fp32_out_and_own_sync_words(wd):
     B, H, I, E, K = 2, 4096, 192, 128, 8
     wgu, wdn = weights(H, I, E, 41)
     x, ids, scale = W.make_device_activations(B, H, E, K, "uniform", 8500)
-    sync = torch.zeros(2, dtype=torch.int32, device="cuda")
+    sync = torch.zeros(1, dtype=torch.int64, device="cuda")
     y32, _, st = run_ffn(capi.FFN_FUSED, x, wgu, wdn, ids, scale, sync=sync, out_fp32=True)
     assert st == 0
-    assert sync[0].item() == 0 and sync[1].item() == 1, "barrier words: count reset, generation +1"
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    assert sync.item() == G, "barrier counter: one arrival per CTA (one CTA per SM)"
     y16, _, st = run_ffn(capi.FFN_FUSED, x, wgu, wdn, ids, scale, sync=sync)
-    assert st == 0 and sync[1].item() == 2
+    assert st == 0 and sync.item() == 2 * G
     assert np.array_equal(host_bits(y32.to(torch.bfloat16)), host_bits(y16))
     _, y_ref = oracle(x, wgu, wdn, ids, scale)
     check(host_bits(y16), y_ref, "fp32 output")

@@ -278,14 +278,21 @@ struct NoInit {
 // The grouping follows the outputs-not-experts idea of the reference (no
 // align/permute pass over unsorted topk_ids, csrc/moe_gate_up_3d_batched.cu)
 // but shares each expert's weight stream between the slots routed to it.
-template <bool kScale = false, class Init = NoInit>
+// kMode: ROUTE_ANY, ROUTE_SMALL (the caller guarantees n <= 64 and
+// blockDim.x >= 64: only the one-warp grouping is compiled) or ROUTE_LARGE
+// (n > 64: the one-warp grouping is left out).  Less code to fetch on a
+// launch's cold start.
+enum RouteMode : int { ROUTE_ANY = 0, ROUTE_SMALL = 1, ROUTE_LARGE = 2 };
+template <bool kScale = false, class Init = NoInit, int kMode = ROUTE_ANY>
 __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict__ topk_ids,
                                    int n, int E, int K, bool dedup, int cap, uint32_t* status,
                                    Init init = Init(), const float* __restrict__ scale = nullptr,
                                    float* s_scale = nullptr) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int lane = tid & 31, warp = tid >> 5;
-  constexpr int PER = (MAX_SLOTS + 127) / 128;  // slots per thread (blockDim >= 128)
+  // slots per thread (blockDim >= 128, or >= 64 with ROUTE_SMALL)
+  constexpr bool kSmall = kMode == ROUTE_SMALL;
+  constexpr int PER = kSmall ? 1 : (MAX_SLOTS + 127) / 128;
   constexpr int SPER = kScale ? PER : 1;
   int ev[PER];
   float sv[SPER];
@@ -296,7 +303,7 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
     if constexpr (kScale) sv[k] = i < n ? __ldg(scale + i) : 0.f;
   }
   init();
-  if (dedup) {
+  if (!kSmall && dedup) {
     for (int e = tid; e <= E; e += nt) {
       r.mask[e] = 0ull;
       r.cnt[e] = 0;
@@ -326,7 +333,7 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
     __syncthreads();
     return;
   }
-  if (n <= 64) {
+  if (kMode != ROUTE_LARGE && (kSmall || n <= 64)) {
     // Small launch: one warp groups all slots (first-appearance order of
     // the experts, members in slot order) with shared-memory atomics on the
     // touched buckets only and ballot/shuffle scans: one block barrier.
@@ -395,6 +402,7 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
     __syncthreads();
     return;
   }
+  if constexpr (kSmall) return;  // not reached: n <= 64
   // Token masks; an expert (or the invalid bucket) twice in one token, or
   // more than 64 tokens, sends the launch to the ordered warp pass.
   const int ntok = n / K;

@@ -93,6 +93,10 @@ __host__ inline int down_tc_smem_bytes(int stages, int sc, int nbuf, int I, int 
          CTRL_INTS * 4 + route_smem_bytes(n, E, true);
 }
 
+// kTP: the fused all-reduce variant (tp.world > 1); the plain kernel carries
+// none of its code.  kRoute: routing code compiled for this launch's slot
+// count (RouteMode).
+template <bool kTP, int kRoute>
 __global__ void __launch_bounds__(DTC_THREADS, 1)
     moe_down_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const DownTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -125,7 +129,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int rank = CL > 1 ? (int)cluster_ctarank() : 0;
   const int j0 = ((int)blockIdx.x / CL) * DTC_M;
-  const uint32_t tp_ep = a.tp.world > 1 ? a.tp.epochs[blockIdx.x] + 1u : 0u;
+  const uint32_t tp_ep = kTP && a.tp.world > 1 ? a.tp.epochs[blockIdx.x] + 1u : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -153,7 +157,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   for (int i = threadIdx.x; i < a.B * DTC_M; i += blockDim.x) Y[i] = 0.f;
   // h, topk_scale (and possibly topk_ids) come from the preceding kernel.
   pdl_wait_primary();
-  route_build<true>(r, a.ids, n, a.E, a.K, true, DTC_N, a.status, NoInit(), a.scale,
+  route_build<true, NoInit, kRoute>(r, a.ids, n, a.E, a.K, true, DTC_N, a.status, NoInit(), a.scale,
                     s_scale);  // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -189,6 +193,26 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
     bool ok = true;
+    if (nst == 1) {
+      // one stage per item (inter <= 256)
+      for (int g = g_first; g < nsg; g = next_item(g)) {
+        const int slot = (int)(it % (uint32_t)S);
+        if (lane == 0) {
+          if (!wait(&wempty[slot], ((it / (uint32_t)S) & 1u) ^ 1u)) {
+            ok = false;
+          } else {
+            uint8_t* st = wring + (size_t)slot * SB;
+            mbar_arrive_expect_tx(&wfull[slot], (uint32_t)(kc * DTC_A_CHUNK));
+            for (int c = 0; c < kc; ++c)
+              tma_load_3d(st + c * DTC_A_CHUNK, &tm_w, c * DTC_BK, j0, r.sg_exp[g], &wfull[slot],
+                          pol);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++it;
+      }
+    } else
     for (int g = g_first; ok && g < nsg; g = next_item(g)) {
       for (int sj = 0; sj < nst; ++sj) {
         const int slot = (int)(it % (uint32_t)S);
@@ -224,6 +248,34 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       uint32_t it = 0, its = 0;  // items, weight stages
       bool issued = false, ok = true;
       const uint32_t idesc = tc_idesc_bf16(DTC_M, DTC_N);
+      if (nst == 1) {
+        // one stage per item (inter <= 256)
+        for (int g = g_first; g < nsg; g = next_item(g)) {
+          const int slot = (int)(it % (uint32_t)S);
+          const int bb = (int)(it % (uint32_t)NB);
+          const int d = (int)(it % (uint32_t)DTC_ND);
+          if (!wait(&wfull[slot], (it / (uint32_t)S) & 1u) ||
+              !wait(&bfull[bb], (it / (uint32_t)NB) & 1u) ||
+              !wait(&dempty[d], ((it / (uint32_t)DTC_ND) & 1u) ^ 1u))
+            break;
+          tc_fence_after();
+          const uint8_t* W = wring + (size_t)slot * SB;
+          const uint8_t* Bt = bring + (size_t)bb * BB;
+          const uint32_t dt = tmem + (uint32_t)(d * DTC_N);
+          for (int c = 0; c < kc; ++c) {
+            const uint64_t ad = tc_desc_sw128(smem_u32(W + c * DTC_A_CHUNK));
+            const uint64_t bd = tc_desc_sw128(smem_u32(Bt + c * DTC_B_CHUNK));
+#pragma unroll
+            for (int kk = 0; kk < DTC_BK / 16; ++kk)
+              tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&wempty[slot]);
+          tc_commit(&bempty[bb]);
+          tc_commit(&dfull[d]);
+          issued = true;
+          ++it;
+        }
+      } else
       for (int g = g_first; ok && g < nsg; g = next_item(g)) {
         const int bb = (int)(it % (uint32_t)NB);
         const int d = (int)(it % (uint32_t)DTC_ND);
@@ -330,7 +382,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   if (CL > 1) cluster_wait();
   const int rpr = DTC_M / CL;   // multiple of 16
   const int q4 = rpr / 4;
-  const bool tp = a.tp.world > 1;
+  const bool tp = kTP && a.tp.world > 1;
   const uint32_t ep = tp_ep;  // this call's epoch (read at kernel start)
   const int slot = (int)(ep & 1u);
   auto recv_at = [&](uint2* buf, int src, int t, int row) {
@@ -357,7 +409,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       acc = *reinterpret_cast<const float4*>(src);
     }
     const float v[4] = {acc.x, acc.y, acc.z, acc.w};
-    if (tp) {
+    if constexpr (kTP) if (tp) {
       // Push (value, epoch) packets of this rank's rows to every rank, then
       // collect every rank's packets of the same rows and add them in rank
       // order.  A packet that does not arrive within the bound counts as 0

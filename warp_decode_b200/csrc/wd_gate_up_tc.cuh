@@ -69,6 +69,8 @@ __host__ inline int gate_up_tc_smem_bytes(int stages, int kch, int npad, int n, 
          route_smem_bytes(n, E, true);
 }
 
+// kRoute: routing code compiled for this launch's slot count (RouteMode).
+template <int kRoute>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     moe_gate_up_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                           const __grid_constant__ CUtensorMap tm_x, const GateUpTcArgs a) {
@@ -131,7 +133,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
     }
   };
-  route_build<false>(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status, setup);  // ends with __syncthreads
+  route_build<false, decltype(setup), kRoute>(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status,
+                                             setup);  // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 

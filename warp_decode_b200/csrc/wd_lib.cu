@@ -41,7 +41,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sm_count = 0;
   int smem_optin = 0;
-  uint32_t* ffn_sync = nullptr;  // library-owned grid-barrier words (g_wd_ffn_sync)
+  unsigned long long* ffn_sync = nullptr;  // library-owned grid-barrier counter (g_wd_ffn_sync)
   bool ready = false;
 };
 
@@ -66,8 +66,11 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
-        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel),
-        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<true, wdb::ROUTE_ANY>),
         reinterpret_cast<const void*>(&wdb::moe_ffn_kernel),
     };
     for (const void* k : kernels) {
@@ -152,8 +155,9 @@ int kernel_path(std::atomic<int>& slot, const char* env) {
 int gate_up_path() { return kernel_path(g_gate_up_path, "WARP_DECODE_GATE_UP"); }
 int down_path() { return kernel_path(g_down_path, "WARP_DECODE_DOWN"); }
 
-// FFN entry point: 0 = automatic (single-launch kernel wherever it applies),
-// 1 = always the two kernels, 2 = single launch wherever it applies.
+// FFN entry point: 0 = automatic (single launch up to WD_FFN_AUTO_MAX_SLOTS
+// routed slots), 1 = always the two kernels, 2 = single launch wherever it
+// applies (up to 64 routed slots).
 // WARP_DECODE_FFN=split|fused sets the initial choice.
 std::atomic<int> g_ffn_path{-1};
 int ffn_path() {
@@ -217,7 +221,9 @@ int gate_up_tc_active_clusters(int cl, int smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int nc = 0;
-  if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_gate_up_tc_kernel, &cfg) !=
+  // All instantiations have the same launch shape and resources.
+  if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>,
+                                     &cfg) !=
       cudaSuccess) {
     cudaGetLastError();
     nc = 0;
@@ -314,7 +320,10 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
   cfg.blockDim = dim3(wdb::TC_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_kernel, tm_w, tm_x, a);
+  cudaError_t err =
+      bn * topk <= 64
+          ? cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_kernel<wdb::ROUTE_SMALL>, tm_w, tm_x, a)
+          : cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>, tm_w, tm_x, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("gate_up (tensor core) launch: ") + cudaGetErrorString(err));
   return WD_OK;
@@ -447,7 +456,9 @@ int down_tc_cluster(const DeviceInfo* dev, int hidden, int smem) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nc = 0;
-    if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_down_tc_kernel, &cfg) !=
+    // Both instantiations have the same launch shape and resources.
+    if (cudaOccupancyMaxActiveClusters(
+            &nc, (const void*)wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>, &cfg) !=
         cudaSuccess) {
       cudaGetLastError();
       continue;
@@ -546,7 +557,10 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel, tm, a);
+  const cudaError_t err =
+      a.tp.world > 1 ? cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<true, wdb::ROUTE_ANY>, tm, a)
+      : n <= 64      ? cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<false, wdb::ROUTE_SMALL>, tm, a)
+                     : cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>, tm, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("down (tensor core) launch: ") + cudaGetErrorString(err));
   return WD_OK;
@@ -652,7 +666,7 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
 
 // ---- single-launch FFN ------------------------------------------------------
 struct FfnPlan {
-  int depth = 0, kc = 0, rc = 0, lpr = 0, rows_max = 0, stage_bytes = 0, xh_bytes = 0;
+  int depth = 0, kc = 0, rc = 0, rows_max = 0, stage_bytes = 0, xh_bytes = 0;
   int smem = 0, grid = 0;
   bool dedup = false;
 };
@@ -681,12 +695,21 @@ bool ffn_fits(const DeviceInfo* dev, int smem) {
   return nb >= 1;
 }
 
+// Routed slots up to which the automatic choice takes the single launch.
+// Measured on B200 (H 4096, I 192, top-8, cold L2): 22.6 / 30.6 / 43.0 us at
+// B = 1 / 2 / 4 against 30.9 / 36.5 / 49.2 us for the two kernels; at B = 8
+// the two kernels (tensor-core down) are as fast (66.7 vs 67.7 us).
+#ifndef WD_FFN_AUTO_MAX_SLOTS
+#define WD_FFN_AUTO_MAX_SLOTS 32
+#endif
+
 // Launch geometry of the single-launch FFN, or false where it does not apply:
-// more than 64 routed slots, E above the dedup table, or x / h of the call
-// too large for shared memory next to a two-slot ring.
-bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int inter, FfnPlan* pl) {
+// more than max_slots routed slots (at most 64), E above the dedup table, or
+// x / h of the call too large for shared memory next to a two-slot ring.
+bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int inter, int max_slots,
+              FfnPlan* pl) {
   const int n = B * topk;
-  if (n < 1 || n > wdb::FFN_MAX_SLOTS) return false;
+  if (n < 1 || n > std::min(max_slots, wdb::FFN_MAX_SLOTS)) return false;
   if (hidden % 8 != 0 || inter % 8 != 0) return false;
   const bool dedup = n > 1;
   if (dedup && E > wdb::MAX_DEDUP_E) return false;
@@ -700,8 +723,6 @@ bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int int
   const int rc_cap = std::max(1, p.stage_bytes / row_bytes);
   const int nch = (p.rows_max + rc_cap - 1) / rc_cap;
   p.rc = (p.rows_max + nch - 1) / nch;
-  const int nvec = inter / 8;
-  p.lpr = nvec <= 32 ? 8 : (nvec <= 64 ? 16 : 32);
   p.xh_bytes = std::max(B * hidden * 2, n * inter * 2);
   p.dedup = dedup;
   const int budget = dev->smem_optin - 2048;
@@ -729,7 +750,7 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
   a.ids = ids;
   a.scale = scale;
   a.h = reinterpret_cast<__nv_bfloat16*>(h);
-  a.sync = sync;
+  a.sync = reinterpret_cast<unsigned long long*>(sync);
   a.out = y;
   a.out_fp32 = out_fp32 ? 1 : 0;
   a.status = status;
@@ -739,7 +760,6 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
   a.stage_bytes = p.stage_bytes;
   a.kc = p.kc;
   a.rc = p.rc;
-  a.lpr = p.lpr;
   a.rows_max = p.rows_max;
   a.xh_bytes = p.xh_bytes;
   cudaLaunchAttribute attr[1];
@@ -863,9 +883,12 @@ int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_do
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   FfnPlan plan;
-  if (ffn_path() != 1 && ffn_plan(dev, B, E, topk, hidden, inter, &plan))
+  const int fp = ffn_path();
+  if (fp != 1 && ffn_plan(dev, B, E, topk, hidden, inter,
+                          fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
     return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
-                      sync ? sync : dev->ffn_sync, y_out, out_fp32, B, E, topk, hidden, inter,
+                      sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, out_fp32, B,
+                      E, topk, hidden, inter,
                       status, reinterpret_cast<cudaStream_t>(stream));
   rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
                                  topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
