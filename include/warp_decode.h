@@ -184,6 +184,22 @@ WD_API int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const voi
                                  int topk, int hidden, int inter, uint32_t* status, void* stream);
 
 /*
+ * wd_moe_ffn_3d_batched without h_buf and sync: allocates nothing.  No
+ * counterpart in the reference.  h and the grid-barrier counter live in a
+ * file-scope static device array of the library (256 B + 128 KiB per
+ * device); calls with B*topk*inter*2 > 131072 bytes return
+ * WD_ERR_UNSUPPORTED.  The array's counter starts zeroed at module load and
+ * needs no reset.  Every call on a device uses the same array, so calls that
+ * overlap in time (other streams) race: serialise them.  The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress) and must not be
+ * made while that device's stream is being captured.
+ */
+WD_API int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, const void* w_down,
+                                         const int32_t* topk_ids, const float* topk_scale,
+                                         void* y_out, int out_fp32, int B, int E, int topk,
+                                         int hidden, int inter, uint32_t* status, void* stream);
+
+/*
  * Kernel choice behind wd_moe_ffn_3d_batched for later calls in this process:
  * 0 = automatic (single launch up to 32 routed slots), 1 = always the two
  * kernels, 2 = single launch wherever it applies (up to 64 routed slots).  WARP_DECODE_FFN=split|fused

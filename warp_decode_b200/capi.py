@@ -46,6 +46,8 @@ _SIGS = {
     "wd_moe_ffn_3d_batched": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                    _P]),
     "wd_set_ffn_path": (_I, [_I]),
+    "wd_moe_ffn_3d_batched_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
+                                           _P]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -116,6 +118,12 @@ def ffn(x, w_gu, w_dn, ids, scale, h, sync, out, out_fp32, B, E, topk, hidden, i
         status=None, stream=0) -> int:
     return lib().wd_moe_ffn_3d_batched(x, w_gu, w_dn, ids, scale, h, sync, out, out_fp32, B, E,
                                        topk, hidden, inter, status, stream)
+
+
+def ffn_noalloc(x, w_gu, w_dn, ids, scale, out, out_fp32, B, E, topk, hidden, inter,
+                status=None, stream=0) -> int:
+    return lib().wd_moe_ffn_3d_batched_noalloc(x, w_gu, w_dn, ids, scale, out, out_fp32, B, E,
+                                               topk, hidden, inter, status, stream)
 
 
 def set_ffn_path(path: int) -> None:

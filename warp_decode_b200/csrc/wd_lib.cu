@@ -27,6 +27,15 @@
 #include "wd_down_tc.cuh"
 #include "wd_ffn.cuh"
 
+// Scratch of wd_moe_ffn_3d_batched_noalloc: [0, 8) the grid-barrier counter
+// (zero at module load; each single-launch call adds one per CTA, so it never
+// needs resetting), [256, 256 + 128 KiB) h of the call (B*topk*inter bf16, at
+// most 64 routed slots x 1024 inter).  One copy per device; calls that overlap
+// in time race on it.
+constexpr size_t kNoallocHeader = 256;
+constexpr size_t kNoallocHBytes = (size_t)64 * 1024 * 2;
+static __device__ __align__(256) unsigned char g_wd_noalloc_scratch[kNoallocHeader + kNoallocHBytes];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -42,6 +51,7 @@ struct DeviceInfo {
   int sm_count = 0;
   int smem_optin = 0;
   unsigned long long* ffn_sync = nullptr;  // library-owned grid-barrier counter (g_wd_ffn_sync)
+  unsigned char* noalloc_scratch = nullptr;  // g_wd_noalloc_scratch, set on first use
   bool ready = false;
 };
 
@@ -890,6 +900,50 @@ int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_do
                       sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, out_fp32, B,
                       E, topk, hidden, inter,
                       status, reinterpret_cast<cudaStream_t>(stream));
+  rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
+                                 topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
+  if (rc) return rc;
+  return down_impl<wdb::W_BF16>(h_buf, reinterpret_cast<const uint8_t*>(w_down), nullptr,
+                                topk_ids, topk_scale, y_out, out_fp32, B, E, topk, hidden, inter,
+                                status, stream);
+}
+
+int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, const void* w_down,
+                                  const int32_t* topk_ids, const float* topk_scale, void* y_out,
+                                  int out_fp32, int B, int E, int topk, int hidden, int inter,
+                                  uint32_t* status, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (hidden % 8 != 0 || inter % 8 != 0)
+    return fail(WD_ERR_SHAPE, "hidden and inter must be multiples of 8 (16-byte weight rows)");
+  if (B == 0) return WD_OK;
+  if ((size_t)B * topk * inter * 2 > kNoallocHBytes)
+    return fail(WD_ERR_UNSUPPORTED, "B*topk*inter*2 exceeds the 131072-byte static scratch");
+  if (!x || !w_gate_up || !w_down || !topk_ids || !topk_scale || !y_out)
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down))
+    return fail(WD_ERR_ALIGNMENT, "x, w_gate_up and w_down must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!dev->noalloc_scratch) {
+      const cudaError_t err =
+          cudaGetSymbolAddress(reinterpret_cast<void**>(&dev->noalloc_scratch), g_wd_noalloc_scratch);
+      if (err != cudaSuccess)
+        return fail(WD_ERR_CUDA, std::string("scratch address: ") + cudaGetErrorString(err));
+    }
+  }
+  uint32_t* sync = reinterpret_cast<uint32_t*>(dev->noalloc_scratch);
+  void* h_buf = dev->noalloc_scratch + kNoallocHeader;
+  FfnPlan plan;
+  const int fp = ffn_path();
+  if (fp != 1 && ffn_plan(dev, B, E, topk, hidden, inter,
+                          fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
+    return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf, sync, y_out,
+                      out_fp32, B, E, topk, hidden, inter, status,
+                      reinterpret_cast<cudaStream_t>(stream));
   rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
                                  topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
   if (rc) return rc;
