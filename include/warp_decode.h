@@ -200,6 +200,21 @@ WD_API int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, c
                                          int hidden, int inter, uint32_t* status, void* stream);
 
 /*
+ * Router producer (no counterpart in the reference, which takes topk_ids and
+ * topk_scale as inputs): from router logits [B, E] (bf16, or fp32 when
+ * logits_fp32 != 0) write
+ *   topk_ids     [B, topk] int32 = the topk largest logits of each row, in
+ *                descending order; equal logits in ascending expert order
+ *   topk_weights [B, topk] fp32  = renormalize ? softmax over the selected
+ *                logits : softmax over all E logits, at the selected ids
+ * NaN logits rank below every number.  1 <= topk <= min(E, 32), E <= 1024.
+ * Asynchronous on `stream`; the outputs feed wd_moe_*_3d_batched directly.
+ */
+WD_API int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
+                              float* topk_weights, int B, int E, int topk, int renormalize,
+                              void* stream);
+
+/*
  * Kernel choice behind wd_moe_ffn_3d_batched for later calls in this process:
  * 0 = automatic (single launch up to 32 routed slots), 1 = always the two
  * kernels, 2 = single launch wherever it applies (up to 64 routed slots).  WARP_DECODE_FFN=split|fused

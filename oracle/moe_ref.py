@@ -28,6 +28,13 @@ axis, elements rounded to nearest-even E4M3 with saturation at 448, scale
 stored as a biased ue8m0 byte), which the reference lists as future work
 (README.md:294-308) and which therefore has no reference source to follow.
 
+The router producer (``router_topk``) has no reference source either (the
+reference takes topk_ids / topk_scale as inputs); it restates the usual MoE
+router: top-k of the logits (softmax is monotonic), weights = softmax over
+the selected logits when renormalised, else softmax over all logits at the
+selected ids.  Its parity is "unpinned" against the reference (nothing to
+pin to) and checked against torch.topk / torch.softmax in the tests.
+
 Parity pins: ``tests/golden/`` holds outputs of the reference's own
 ``reference_gate_up`` / ``reference_down`` and of its FP32 formula, generated
 by ``tests/golden/make_golden.py``; ``tests/test_oracle.py`` checks this module
@@ -39,7 +46,7 @@ import numpy as np
 
 __all__ = [
     "bf16_to_f32", "f32_to_bf16", "silu_f32", "gate_up", "down", "moe_ffn",
-    "e4m3_to_f32", "f32_to_e4m3", "mx_quantize", "mx_dequantize", "E4M3_MAX",
+    "e4m3_to_f32", "f32_to_e4m3", "mx_quantize", "mx_dequantize", "E4M3_MAX", "router_topk",
 ]
 
 E4M3_MAX = 448.0
@@ -224,3 +231,29 @@ def mx_dequantize(q, scale, block: int = 32) -> np.ndarray:
     vals = e4m3_to_f32(q).reshape(*q.shape[:-1], K // block, block).astype(np.float64)
     s = np.exp2(np.asarray(scale, dtype=np.float64) - 127.0)
     return (vals * s[..., None]).reshape(q.shape).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# router producer (top-k + softmax)
+# ---------------------------------------------------------------------------
+def router_topk(logits, topk: int, renormalize: bool = True):
+    """(ids int32 [B, k], weights float32 [B, k]) from logits [B, E] (float32 values).
+
+    Order: descending logit, equal logits by ascending expert id; NaN ranks
+    below every number.  Weights: exp(l - l_max) / sum, the sum over the k
+    selected (renormalize) or over all E; float64 arithmetic, float32 result.
+    """
+    lg = np.asarray(logits, dtype=np.float64)
+    lg = np.where(np.isnan(lg), -np.inf, lg)
+    B, E = lg.shape
+    ids = np.zeros((B, topk), dtype=np.int32)
+    w = np.zeros((B, topk), dtype=np.float32)
+    for b in range(B):
+        order = sorted(range(E), key=lambda e: (-lg[b, e], e))[:topk]
+        ids[b] = order
+        sel = lg[b, order]
+        ref = sel[0] if np.isfinite(sel[0]) else 0.0
+        num = np.exp(sel - ref)
+        den = num.sum() if renormalize else np.exp(lg[b] - ref).sum()
+        w[b] = (num / den) if den > 0 else np.full(topk, 1.0 / topk)
+    return ids, w

@@ -48,6 +48,7 @@ _SIGS = {
     "wd_set_ffn_path": (_I, [_I]),
     "wd_moe_ffn_3d_batched_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                            _P]),
+    "wd_moe_router_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -124,6 +125,11 @@ def ffn_noalloc(x, w_gu, w_dn, ids, scale, out, out_fp32, B, E, topk, hidden, in
                 status=None, stream=0) -> int:
     return lib().wd_moe_ffn_3d_batched_noalloc(x, w_gu, w_dn, ids, scale, out, out_fp32, B, E,
                                                topk, hidden, inter, status, stream)
+
+
+def router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize, stream=0) -> int:
+    return lib().wd_moe_router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize,
+                                    stream)
 
 
 def set_ffn_path(path: int) -> None:

@@ -197,6 +197,25 @@ torch::Tensor moe_ffn_3d_batched(torch::Tensor x, torch::Tensor w_gate_up, torch
   return out;
 }
 
+// Router producer: (topk_ids int32 [B, topk], topk_weights fp32 [B, topk]).
+std::tuple<torch::Tensor, torch::Tensor> moe_router_topk(torch::Tensor logits, int64_t topk,
+                                                         bool renormalize) {
+  CHECK_CUDA(logits); CHECK_CONTIG(logits);
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kFloat,
+              "logits must be bf16 or fp32");
+  TORCH_CHECK(logits.dim() == 2, "logits must be [B, E]");
+  const int B = to_int(logits.size(0), "B");
+  const int E = to_int(logits.size(1), "E");
+  const int K = to_int(topk, "topk");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  auto ids = torch::empty({B, K}, logits.options().dtype(at::kInt));
+  auto w = torch::empty({B, K}, logits.options().dtype(at::kFloat));
+  check_rc(wd_moe_router_topk(logits.data_ptr(), logits.scalar_type() == at::kFloat ? 1 : 0,
+                              ids.data_ptr<int32_t>(), w.data_ptr<float>(), B, E, K,
+                              renormalize ? 1 : 0, stream_ptr()));
+  return {ids, w};
+}
+
 int64_t status(bool clear, int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   uint32_t v = 0;
@@ -232,6 +251,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "gate_up + silu*up + down + top-k weighted sum in one call (one launch for B*topk <= 64)",
         py::arg("x"), py::arg("w_gate_up"), py::arg("w_down"), py::arg("topk_ids"),
         py::arg("topk_scale"), py::arg("fp32_out") = false);
+  m.def("moe_router_topk", &moe_router_topk,
+        "top-k experts and routing weights from router logits [B, E] (bf16/fp32)",
+        py::arg("logits"), py::arg("topk"), py::arg("renormalize") = true);
   m.def("status", &status, "Read (and clear) the device status word of the library",
         py::arg("clear") = true, py::arg("device") = 0);
   m.def("set_gate_up_path", &set_gate_up_path,

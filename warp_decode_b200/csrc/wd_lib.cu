@@ -26,6 +26,7 @@
 #include "wd_gate_up_tc.cuh"
 #include "wd_down_tc.cuh"
 #include "wd_ffn.cuh"
+#include "wd_router.cuh"
 
 // Scratch of wd_moe_ffn_3d_batched_noalloc: [0, 8) the grid-barrier counter
 // (zero at module load; each single-launch call adds one per CTA, so it never
@@ -863,6 +864,36 @@ int wd_set_down_path(int path) {
   g_last_error.clear();
   if (path < 0 || path > 2) return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (simt) or 2 (tc)");
   g_down_path.store(path);
+  return WD_OK;
+}
+
+int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
+                       float* topk_weights, int B, int E, int topk, int renormalize,
+                       void* stream) {
+  g_last_error.clear();
+  if (B < 0) return fail(WD_ERR_SHAPE, "B must be >= 0");
+  if (E < 1 || topk < 1 || topk > E) return fail(WD_ERR_SHAPE, "need 1 <= topk <= E");
+  if (E > wdb::ROUTER_PER * 32 || topk > wdb::ROUTER_MAX_K)
+    return fail(WD_ERR_UNSUPPORTED, "router supports E <= 1024 and topk <= 32");
+  if (B == 0) return WD_OK;
+  if (!logits || !topk_ids || !topk_weights) return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(logits) & (logits_fp32 ? 3u : 1u)) != 0 ||
+      (reinterpret_cast<uintptr_t>(topk_ids) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(topk_weights) & 3u) != 0)
+    return fail(WD_ERR_ALIGNMENT, "logits / topk_ids / topk_weights misaligned for their type");
+  wdb::RouterArgs a;
+  a.logits = logits;
+  a.logits_fp32 = logits_fp32 ? 1 : 0;
+  a.ids = topk_ids;
+  a.weights = topk_weights;
+  a.B = B; a.E = E; a.K = topk;
+  a.renormalize = renormalize ? 1 : 0;
+  const unsigned grid = (unsigned)((B + wdb::ROUTER_WARPS - 1) / wdb::ROUTER_WARPS);
+  wdb::moe_router_topk_kernel<<<grid, wdb::ROUTER_WARPS * 32, 0,
+                                reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return fail(WD_ERR_CUDA, std::string("router launch: ") + cudaGetErrorString(err));
   return WD_OK;
 }
 
