@@ -49,6 +49,8 @@ _SIGS = {
     "wd_moe_ffn_3d_batched_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                            _P]),
     "wd_moe_router_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P]),
+    "wd_moe_ffn_3d_batched_allreduce": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
+                                             _P, _P, _P]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -163,6 +165,22 @@ def tp_comm_open(comm: int, handles: bytes) -> None:
 
 def tp_comm_destroy(comm: int) -> None:
     check(lib().wd_tp_comm_destroy(comm))
+
+
+def torch_ffn_allreduce(x, w_gu, w_dn, ids, scale, comm):
+    """bf16 y[B, hidden] = sum over the group's ranks of this rank's FFN shard."""
+    import torch
+
+    B, K = ids.shape
+    E, two_i, H = w_gu.shape
+    I = two_i // 2
+    h = torch.empty(B * K, I, dtype=torch.bfloat16, device=x.device)
+    y = torch.empty(B, H, dtype=torch.bfloat16, device=x.device)
+    check(lib().wd_moe_ffn_3d_batched_allreduce(x.data_ptr(), w_gu.data_ptr(), w_dn.data_ptr(),
+                                                ids.data_ptr(), scale.data_ptr(), h.data_ptr(),
+                                                None, y.data_ptr(), B, E, K, H, I, comm, None,
+                                                _stream()))
+    return y
 
 
 def torch_down_allreduce(h, w, ids, scale, comm):

@@ -48,8 +48,13 @@ constexpr uint32_t DTC_TMEM_COLS = DTC_ND * DTC_N < 32 ? 32 : DTC_ND * DTC_N;
 // buffer holds [2 slots][world][max_tokens][H] packets of 8 bytes: the FP32
 // partial and the epoch of the call that wrote it, stored together by one
 // 8-byte store, so a reader that sees the epoch sees the value (no fences,
-// no separate flags).  epochs[cta] counts this rank's calls per CTA; slot =
-// epoch & 1 keeps a rank that is one call ahead off the slot still being read.
+// no separate flags).  epochs[] counts this rank's calls: CTA c of a call
+// reads epochs[c] and at the end writes the new count to epochs[c],
+// epochs[c + grid], ..., so every entry advances by one per call whatever grid
+// the kernel used (the single-launch FFN and this kernel partition the rows
+// differently; a packet left by either never carries a current epoch).
+// slot = epoch & 1 keeps a rank that is one call ahead off the slot still
+// being read.
 constexpr int TP_MAX_WORLD = 8;
 struct TpArgs {
   int world;                        // <= 1: no fused all-reduce
@@ -463,7 +468,8 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       }
     }
   }
-  if (tp && threadIdx.x == 0) a.tp.epochs[blockIdx.x] = ep;
+  if (tp && threadIdx.x == 0)
+    for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += (int)gridDim.x) a.tp.epochs[c2] = ep;
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile
 }
 

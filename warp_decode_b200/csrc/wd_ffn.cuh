@@ -27,6 +27,11 @@
 //  * Phase 2 (down): CTA c owns output rows [c*H/G, (c+1)*H/G) for every
 //    token; per-warp FP32 tiles summed in a fixed order (deterministic, no
 //    atomics on y).
+//  * Tensor parallelism (kTP): the CTA's FP32 rows are this rank's partial
+//    sums; they go to every rank as (value, epoch) packets over NVLink peer
+//    stores and the CTA adds every rank's packets of its rows in rank order
+//    (the exchange of the tcgen05 down kernel, TpArgs): y is the all-reduced
+//    bf16 output, identical bits on every rank, with no other launch.
 //  * Short code on the launch's critical path: after an L2 flush the kernel's
 //    instructions come from DRAM, and each taken branch into code not yet
 //    fetched costs about a DRAM latency.  Routing compiles only the
@@ -35,6 +40,7 @@
 #pragma once
 
 #include "wd_down.cuh"
+#include "wd_down_tc.cuh"
 #include "wd_tc.cuh"
 
 namespace wdb {
@@ -58,6 +64,7 @@ struct FfnArgs {
   int rc;           // down: weight rows per chunk
   int rows_max;     // down: max output rows per CTA (ceil(H / gridDim.x))
   int xh_bytes;     // bytes of the shared x (phase 1) / h (phase 2) region
+  TpArgs tp;        // fused all-reduce (kTP): y = bf16 sum over the group's ranks
 };
 
 constexpr int FFN_THREADS = NWARPS * 32;
@@ -161,6 +168,7 @@ __device__ __forceinline__ void ffn_down_stage(const uint8_t* st, int row_bytes,
   }
 }
 
+template <bool kTP>
 __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a) {
   constexpr int NCW = NWARPS;
   constexpr int WB = 2;  // bf16 weights
@@ -194,6 +202,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = (int)gridDim.x;
+  const uint32_t tp_ep = kTP ? a.tp.epochs[blockIdx.x] + 1u : 0u;  // this call's epoch
 
   // Barrier counter at entry (used at the barrier): every earlier launch
   // added exactly G arrivals and this CTA has not arrived yet, so
@@ -433,10 +442,60 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   __syncthreads();
   if (ctrl[0]) {
     // A wait gave up: let issued but unconsumed copies land, then leave
-    // without writing y (the status word says so).
+    // without writing y (the status word says so).  With the fused
+    // all-reduce the call still counts (epochs stay in step with the peers,
+    // which time out on this rank's missing packets).
     if (lane == 0)
       for (int q = ctrl[16 + warp]; q < ctrl[8 + warp]; ++q)
         if (!mbar_wait(&my_full[q % depth], (uint32_t)(q / depth) & 1u)) break;
+    if (kTP && threadIdx.x == 0)
+      for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += G) a.tp.epochs[c2] = tp_ep;
+    return;
+  }
+  if constexpr (kTP) {
+    // Push this rank's partial rows to every rank, then add every rank's
+    // packets of the same rows in rank order (bounded waits: a packet that
+    // does not arrive within 2 s counts as 0 and raises WD_STATUS_WAIT_TIMEOUT).
+    const TpArgs& tp = a.tp;
+    const int slot = (int)(tp_ep & 1u);
+    auto recv_at = [&](uint2* buf, int src, int t, int row) {
+      return buf + (((size_t)(slot * tp.world + src) * tp.max_tokens + t) * H + row);
+    };
+    for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
+      const int b = i / nrows;
+      const int lr = i - b * nrows;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) v += tiles[(size_t)w * tile + b * a.rows_max + lr];
+      for (int r = 0; r < tp.world; ++r)
+        st_volatile_u2(recv_at(tp.recv[r], tp.rank, b, r0 + lr), __float_as_uint(v), tp_ep);
+    }
+    bool ok = true;
+    for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
+      const int b = i / nrows;
+      const int lr = i - b * nrows;
+      float sum = 0.f;
+      for (int r = 0; r < tp.world && ok; ++r) {
+        const uint2* pk = recv_at(tp.recv[tp.rank], r, b, r0 + lr);
+        uint2 v = ld_volatile_u2(pk);
+        if (v.y != tp_ep) {
+          const uint64_t t0 = globaltimer_ns();
+          do {
+            v = ld_volatile_u2(pk);
+            if (v.y != tp_ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+              raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+              ok = false;
+              break;
+            }
+          } while (v.y != tp_ep);
+        }
+        if (ok) sum += __uint_as_float(v.x);
+      }
+      reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)b * H + r0 + lr] =
+          __float2bfloat16_rn(ok ? sum : 0.f);
+    }
+    if (threadIdx.x == 0)
+      for (int c2 = (int)blockIdx.x; c2 < tp.max_ctas; c2 += G) tp.epochs[c2] = tp_ep;
     return;
   }
   // y = sum of the 8 warp tiles in a fixed order.

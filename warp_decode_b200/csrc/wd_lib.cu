@@ -82,7 +82,8 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<true, wdb::ROUTE_ANY>),
-        reinterpret_cast<const void*>(&wdb::moe_ffn_kernel),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_kernel<false>),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_kernel<true>),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -695,8 +696,9 @@ bool ffn_fits(const DeviceInfo* dev, int smem) {
       if (c[0] == devno && c[1] == smem) return c[2] != 0;
   }
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, wdb::moe_ffn_kernel, wdb::FFN_THREADS,
-                                                    (size_t)smem) != cudaSuccess) {
+  // both instantiations: one CTA per SM of 256 threads, the same shared memory
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, wdb::moe_ffn_kernel<true>,
+                                                    wdb::FFN_THREADS, (size_t)smem) != cudaSuccess) {
     cudaGetLastError();
     nb = 0;
   }
@@ -753,7 +755,7 @@ bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int int
 int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const void* w_gu,
                const void* w_dn, const int32_t* ids, const float* scale, void* h, uint32_t* sync,
                void* y, int out_fp32, int B, int E, int topk, int hidden, int inter,
-               uint32_t* status, cudaStream_t s) {
+               uint32_t* status, cudaStream_t s, const wdb::TpArgs* tp = nullptr) {
   wdb::FfnArgs a;
   a.x = reinterpret_cast<const __nv_bfloat16*>(x);
   a.wgu = reinterpret_cast<const uint8_t*>(w_gu);
@@ -773,6 +775,8 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
   a.rc = p.rc;
   a.rows_max = p.rows_max;
   a.xh_bytes = p.xh_bytes;
+  a.tp = {};
+  if (tp) a.tp = *tp;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
@@ -783,7 +787,8 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel, a);
+  cudaError_t err = tp ? cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel<true>, a)
+                       : cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel<false>, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("ffn launch: ") + cudaGetErrorString(err));
   return WD_OK;
@@ -798,6 +803,18 @@ struct TpComm {
   uint32_t* epochs = nullptr;     // [max_ctas], local only
   void* peer[wdb::TP_MAX_WORLD] = {};  // opened IPC mappings (nullptr for self)
 };
+
+wdb::TpArgs make_tp_args(const TpComm* c) {
+  wdb::TpArgs tp = {};
+  tp.world = c->world;
+  tp.rank = c->rank;
+  tp.max_tokens = c->max_tokens;
+  tp.max_ctas = c->max_ctas;
+  tp.epochs = c->epochs;
+  for (int r = 0; r < c->world; ++r)
+    tp.recv[r] = static_cast<uint2*>(r == c->rank ? c->block : c->peer[r]);
+  return tp;
+}
 
 }  // namespace
 
@@ -1068,14 +1085,7 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
   if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK ||
       (hidden + wdb::DTC_M - 1) / wdb::DTC_M > dev->sm_count)
     return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 1024)");
-  wdb::TpArgs tp = {};
-  tp.world = c->world;
-  tp.rank = c->rank;
-  tp.max_tokens = c->max_tokens;
-  tp.max_ctas = c->max_ctas;
-  tp.epochs = c->epochs;
-  for (int r = 0; r < c->world; ++r)
-    tp.recv[r] = static_cast<uint2*>(r == c->rank ? c->block : c->peer[r]);
+  const wdb::TpArgs tp = make_tp_args(c);
   const int tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), std::min(64, c->max_tokens));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {
@@ -1087,6 +1097,48 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
     if (rc) return rc;
   }
   return WD_OK;
+}
+
+int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up, const void* w_down,
+                                    const int32_t* topk_ids, const float* topk_scale, void* h_buf,
+                                    uint32_t* sync, void* y_out, int B, int E, int topk,
+                                    int hidden, int inter, void* comm, uint32_t* status,
+                                    void* stream) {
+  g_last_error.clear();
+  TpComm* c = static_cast<TpComm*>(comm);
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  if (!c) return fail(WD_ERR_NULL_POINTER, "comm is NULL");
+  if (hidden % 8 != 0 || inter % 8 != 0)
+    return fail(WD_ERR_SHAPE, "hidden and inter must be multiples of 8 (16-byte weight rows)");
+  if (B == 0) return WD_OK;
+  if (!x || !w_gate_up || !w_down || !topk_ids || !topk_scale || !h_buf || !y_out)
+    return fail(WD_ERR_NULL_POINTER, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(w_gate_up) || !aligned16(w_down) || !aligned16(h_buf))
+    return fail(WD_ERR_ALIGNMENT, "x, w_gate_up, w_down and h_buf must be 16-byte aligned");
+  if (sync && (reinterpret_cast<uintptr_t>(sync) & 7u) != 0)
+    return fail(WD_ERR_ALIGNMENT, "sync must be 8-byte aligned");
+  if (hidden != c->hidden) return fail(WD_ERR_SHAPE, "hidden differs from the communicator's");
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && !c->peer[r]) return fail(WD_ERR_UNSUPPORTED, "communicator not opened");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  FfnPlan plan;
+  const int fp = ffn_path();
+  if (fp != 1 && B <= c->max_tokens &&
+      ffn_plan(dev, B, E, topk, hidden, inter,
+               fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan) &&
+      plan.grid <= c->max_ctas) {
+    const wdb::TpArgs tp = make_tp_args(c);
+    return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
+                      sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, 0, B, E,
+                      topk, hidden, inter, status, reinterpret_cast<cudaStream_t>(stream), &tp);
+  }
+  rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
+                                 topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
+  if (rc) return rc;
+  return wd_moe_down_3d_batched_allreduce(h_buf, w_down, topk_ids, topk_scale, y_out, B, E, topk,
+                                          hidden, inter, comm, status, stream);
 }
 
 int wd_status_read(uint32_t* value, int clear) {

@@ -106,6 +106,10 @@ class FusedAllReduce:
     def down(self, h, w, ids, scale):
         return self.capi.torch_down_allreduce(h, w, ids, scale, self.comm)
 
+    def ffn(self, x, w_gu, w_dn, ids, scale):
+        """gate_up + down + all-reduce; one kernel launch for small batches."""
+        return self.capi.torch_ffn_allreduce(x, w_gu, w_dn, ids, scale, self.comm)
+
     def close(self):
         if self.comm:
             self.capi.tp_comm_destroy(self.comm)
@@ -155,6 +159,8 @@ class TensorParallelMoE:
     def __call__(self, x, topk_ids, topk_scale):
         if (self.fused is not None and self.world > 1 and self.s_dn is None
                 and self.fused.applies(x.shape[0])):
+            if self.s_gu is None:
+                return self.fused.ffn(x, self.w_gu, self.w_dn, topk_ids, topk_scale)
             h = self.kernels.gate_up(x, self.w_gu, topk_ids, self.s_gu)
             return self.fused.down(h, self.w_dn, topk_ids, topk_scale)
         part = self.partial(x, topk_ids, topk_scale)
