@@ -361,33 +361,39 @@ def run_ours(args, rank, local_rank, world):
                               "per-launch CUDA-event durations (one launch per batch size)"}
 
         # ---- end to end through the public API with host buffers ----
-        pinned = {}
+        # x, topk_ids and topk_scale of a call sit in one pinned host buffer
+        # and go to the device in one copy (views of one device buffer).
+        packed = {}
         for B in batches:
             c = cases[B]
-            pinned[B] = (c.x.cpu().pin_memory(), c.ids.cpu().pin_memory(), c.scale.cpu().pin_memory(),
-                         torch.empty(B, H, dtype=torch.bfloat16).pin_memory())
+            parts = [c.x.cpu().view(torch.uint8).reshape(-1), c.ids.cpu().view(torch.uint8).reshape(-1),
+                     c.scale.cpu().view(torch.uint8).reshape(-1)]
+            host = torch.cat(parts).pin_memory()
+            dbuf = torch.empty_like(host, device=dev)
+            xb, ib = parts[0].numel(), parts[1].numel()
+            xd = dbuf[:xb].view(torch.bfloat16).view(B, H)
+            idd = dbuf[xb:xb + ib].view(torch.int32).view(B, K)
+            scd = dbuf[xb + ib:].view(torch.float32).view(B, K)
+            packed[B] = (host, dbuf, xd, idd, scd, torch.empty(B, H, dtype=torch.bfloat16).pin_memory())
         h2d = sum(B * H * 2 + B * K * 8 for B in batches)
         d2h = sum(B * H * 2 for B in batches)
         reps = max(5, min(args.steps, 30))
         e2e_ts = []
-        xd = {B: torch.empty_like(cases[B].x) for B in batches}
-        idd = {B: torch.empty_like(cases[B].ids) for B in batches}
-        scd = {B: torch.empty_like(cases[B].scale) for B in batches}
         for r in range(reps + 2):
             row = []
             for B in batches:
-                xh, ih, sh, yh = pinned[B]
+                host, dbuf, xd, idd, scd, yh = packed[B]
                 flush()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(cur)
-                xd[B].copy_(xh, non_blocking=True)
-                idd[B].copy_(ih, non_blocking=True)
-                scd[B].copy_(sh, non_blocking=True)
+                dbuf.copy_(host, non_blocking=True)
                 if world == 1:
-                    y = wd.moe_ffn_3d_batched(xd[B], w_gu, w_dn, idd[B], scd[B])
+                    y = wd.moe_ffn_3d_batched(xd, w_gu, w_dn, idd, scd)
+                elif fused is not None and fused.applies(B):
+                    y = fused.ffn(xd, w_gu, w_dn, idd, scd)
                 else:
-                    h = wd.moe_gate_up_3d_batched(xd[B], w_gu, idd[B])
-                    y = wd.moe_down_3d_batched_partial(h, w_dn, idd[B], scd[B], B)
+                    h = wd.moe_gate_up_3d_batched(xd, w_gu, idd)
+                    y = wd.moe_down_3d_batched_partial(h, w_dn, idd, scd, B)
                     dist.all_reduce(y)
                     y = y.to(torch.bfloat16)
                 yh.copy_(y, non_blocking=True)
@@ -404,10 +410,10 @@ def run_ours(args, rank, local_rank, world):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "method": ("eager torch API (moe_ffn_3d_batched) per call"
                           if world == 1 else
-                          "eager torch API (moe_gate_up_3d_batched + moe_down_3d_batched_partial "
-                          "+ all_reduce) per call") +
-                         ", pinned host inputs copied in and y copied out inside the timed window, "
-                         "L2 flushed before each call"}
+                          "eager torch API (FusedAllReduce.ffn, or moe_gate_up_3d_batched + "
+                          "moe_down_3d_batched_partial + all_reduce above the fused size) per call") +
+                         ", x / topk_ids / topk_scale copied in from one pinned host buffer and y "
+                         "copied out inside the timed window, L2 flushed before each call"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
