@@ -496,20 +496,20 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
     }
     if (threadIdx.x == 0)
       for (int c2 = (int)blockIdx.x; c2 < tp.max_ctas; c2 += G) tp.epochs[c2] = tp_ep;
-    return;
-  }
-  // y = sum of the 8 warp tiles in a fixed order.
-  for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
-    const int b = i / nrows;
-    const int lr = i - b * nrows;
-    float v = 0.f;
+  } else {
+    // y = sum of the 8 warp tiles in a fixed order.
+    for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
+      const int b = i / nrows;
+      const int lr = i - b * nrows;
+      float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < NCW; ++w) v += tiles[(size_t)w * tile + b * a.rows_max + lr];
-    const size_t o = (size_t)b * H + r0 + lr;
-    if (a.out_fp32)
-      reinterpret_cast<float*>(a.out)[o] = v;
-    else
-      reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(v);
+      for (int w = 0; w < NCW; ++w) v += tiles[(size_t)w * tile + b * a.rows_max + lr];
+      const size_t o = (size_t)b * H + r0 + lr;
+      if (a.out_fp32)
+        reinterpret_cast<float*>(a.out)[o] = v;
+      else
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(v);
+    }
   }
 }
 
