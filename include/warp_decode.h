@@ -149,7 +149,7 @@ WD_API int wd_set_gate_up_path(int path);
 /*
  * The same choice for wd_moe_down_3d_batched (bf16 weights): 0 = automatic
  * (tcgen05 kernel from 2 tokens per call), 1 = SIMT kernel only, 2 = tensor-
- * core kernel wherever it applies (inter <= 1024, E <= 1024, hidden <= 128 x
+ * core kernel wherever it applies (inter <= 2048, E <= 1024, hidden <= 128 x
  * the SM count).  WARP_DECODE_DOWN=simt|tc sets the initial choice.  No
  * counterpart in the reference.
  */
@@ -242,7 +242,7 @@ WD_API int wd_set_ffn_path(int path);
  *      NVLink peer stores (no fences, no flags); a peer that does not arrive
  *      within 2 s ends the wait with WD_STATUS_WAIT_TIMEOUT (the output is
  *      then zeros), never a hang.  Needs the tensor-core down kernel's shapes
- *      (inter <= 1024, E <= 1024) and B <= max_tokens per call chunk.
+ *      (inter <= 2048, E <= 1024) and B <= max_tokens per call chunk.
  *   4. wd_tp_comm_destroy(comm) after all ranks are done with it.
  */
 WD_API int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, void** comm,

@@ -90,7 +90,9 @@ def test_qwen3_tp8_both_paths(wd, B):
     (5, 6, 6, 128, 64, "randint"),      # repeated ids inside a token (fixed add order)
     (100, 64, 8, 512, 64, "uniform"),   # B*topk > 512: two launches
     (4, 2048, 8, 256, 64, "uniform"),   # E > 1024: SIMT path
-    (2, 16, 4, 512, 1544, "uniform"),   # inter > 1024: SIMT path
+    (2, 16, 4, 512, 1544, "uniform"),   # 25 K chunks (last partial) in h slices of 4
+    (2, 16, 4, 512, 2056, "uniform"),   # inter > 2048: SIMT path
+    (16, 64, 8, 1024, 1536, "uniform"), # Qwen3-235B full width (TP1): 6 stages per item
     (6, 16, 4, 512, 1000, "uniform"),   # 16 K chunks over 4 weight stages, last chunk partial
     (9, 32, 8, 1024, 512, "randint"),   # 2 weight stages per item, repeated ids
     (8, 256, 8, 7168, 256, "zipf"),     # DeepSeek-V3 TP=8 shard: 56 tiles, clusters of 2

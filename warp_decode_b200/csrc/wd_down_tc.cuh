@@ -13,16 +13,17 @@
 //  * Per item (one expert, at most DTC_N of its routed slots):
 //      A = the expert's 128 weight rows of the tile (M = 128, K = inter),
 //          one 3-D TMA box per 64-wide K chunk (16 KB each), up to 4
-//          chunks per ring stage (inter up to 1024: several stages);
+//          chunks per ring stage (inter up to 2048: several stages);
 //      B = the members' h rows (N = 16), gathered by the gather warps into
-//          the 128-byte-swizzled K-major layout;
+//          the 128-byte-swizzled K-major layout one weight stage's K range
+//          at a time (h slices: shared memory no longer grows with inter);
 //      D[j, c] (TMEM lane j, column c) = row j . h[member c].
 //  * Epilogue warps add topk_scale[c] * D[j, c] into Y[token(c)][j] in
 //    shared memory, one thread per row, members in slot order (so repeated
 //    tokens add in a fixed order).
 //  * Warp roles: 0 = weight TMA producer, 1 = TMEM allocator + MMA issuer,
-//    2..5 = gather (one item each in flight), 6..9 = epilogue (TMEM lane
-//    quarter warp % 4).  Weight stages, B buffers and D buffers are rings
+//    2..5 = gather (one h slice each in flight), 6..9 = epilogue (TMEM lane
+//    quarter warp % 4).  Weight stages, h slices and D buffers are rings
 //    with full/empty mbarriers; every wait is bounded.
 #pragma once
 
@@ -33,7 +34,7 @@ namespace wdb {
 
 constexpr int DTC_M = 128;                       // output rows per tile (MMA M)
 constexpr int DTC_BK = 64;                       // K elements per chunk (128-byte rows)
-constexpr int DTC_MAXKC = 16;                    // inter <= 1024
+constexpr int DTC_MAXKC = 32;                    // inter <= 2048
 constexpr int DTC_SC = 4;                        // max K chunks per weight stage
 constexpr int DTC_N = 16;                        // members per item (MMA N)
 constexpr int DTC_ND = 4;                        // TMEM accumulator buffers
@@ -83,7 +84,8 @@ struct DownTcArgs {
   int B, E, K, H, I;
   int stages;              // weight ring depth
   int sc;                  // K chunks per weight stage (<= DTC_SC)
-  int nbuf;                // h buffers, >= DTC_GW (a gather warp is at most one
+  int nbuf;                // h slices (the K range of one weight stage of one
+                           // item), >= DTC_GW (a gather warp is at most one
                            // ring turn ahead, so mbarrier parities cannot alias)
   int cl;                  // CTAs per cluster (1, 2, 4 or 8)
   TpArgs tp;               // fused all-reduce (tp.world > 1): out = bf16 sum over ranks
@@ -93,7 +95,8 @@ __host__ __device__ inline int down_tc_kc(int I) { return (I + DTC_BK - 1) / DTC
 
 __host__ inline int down_tc_smem_bytes(int stages, int sc, int nbuf, int I, int B, int n, int E) {
   const int kc = down_tc_kc(I);
-  return 1024 + stages * sc * DTC_A_CHUNK + nbuf * kc * DTC_B_CHUNK + B * DTC_M * 4 +
+  (void)kc;
+  return 1024 + stages * sc * DTC_A_CHUNK + nbuf * sc * DTC_B_CHUNK + B * DTC_M * 4 +
          ((n * 4 + 127) / 128) * 128 + (2 * stages + 2 * nbuf + 2 * DTC_ND + 1) * 8 + 16 +
          CTRL_INTS * 4 + route_smem_bytes(n, E, true);
 }
@@ -114,7 +117,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int SC = a.sc;              // K chunks per weight stage
   const int nst = (kc + SC - 1) / SC;  // weight stages per item
   const int SB = SC * DTC_A_CHUNK;  // bytes of one weight stage
-  const int BB = kc * DTC_B_CHUNK;  // bytes of one h buffer
+  const int BB = SC * DTC_B_CHUNK;  // bytes of one h slice (one weight stage's K range)
   uint8_t* wring = base;
   uint8_t* bring = wring + (size_t)S * SB;
   float* Y = reinterpret_cast<float*>(bring + (size_t)NB * BB);  // [B][128]
@@ -282,33 +285,33 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         }
       } else
       for (int g = g_first; ok && g < nsg; g = next_item(g)) {
-        const int bb = (int)(it % (uint32_t)NB);
         const int d = (int)(it % (uint32_t)DTC_ND);
-        if (!wait(&bfull[bb], (it / (uint32_t)NB) & 1u) ||
-            !wait(&dempty[d], ((it / (uint32_t)DTC_ND) & 1u) ^ 1u))
-          break;
-        tc_fence_after();
-        const uint8_t* Bt = bring + (size_t)bb * BB;
+        if (!wait(&dempty[d], ((it / (uint32_t)DTC_ND) & 1u) ^ 1u)) break;
         const uint32_t dt = tmem + (uint32_t)(d * DTC_N);
         for (int sj = 0; sj < nst; ++sj, ++its) {
           const int slot = (int)(its % (uint32_t)S);
-          if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u)) { ok = false; break; }
+          const int hb = (int)(its % (uint32_t)NB);
+          if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u) ||
+              !wait(&bfull[hb], (its / (uint32_t)NB) & 1u)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint8_t* W = wring + (size_t)slot * SB;
+          const uint8_t* Bt = bring + (size_t)hb * BB;
           const int c0 = sj * SC, nc = min(SC, kc - c0);
           for (int cc = 0; cc < nc; ++cc) {
-            const int c = c0 + cc;
             const uint64_t ad = tc_desc_sw128(smem_u32(W + cc * DTC_A_CHUNK));
-            const uint64_t bd = tc_desc_sw128(smem_u32(Bt + c * DTC_B_CHUNK));
+            const uint64_t bd = tc_desc_sw128(smem_u32(Bt + cc * DTC_B_CHUNK));
 #pragma unroll
             for (int kk = 0; kk < DTC_BK / 16; ++kk)
-              tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, (c | kk) != 0 ? 1u : 0u);
+              tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, ((c0 + cc) | kk) != 0 ? 1u : 0u);
           }
           tc_commit(&wempty[slot]);
+          tc_commit(&bempty[hb]);
           issued = true;
         }
         if (!ok) break;
-        tc_commit(&bempty[bb]);
         tc_commit(&dfull[d]);
         ++it;
       }
@@ -321,29 +324,57 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     }
     __syncwarp();
   } else if (warp < 2 + DTC_GW) {
-    // ---------------- gather: h rows of item it, warp it % DTC_GW --------
+    // -------- gather: h slice of stage its (K range of one weight stage of
+    // one item), warp its % DTC_GW --------
     const int gw = warp - 2;
     const int vecs = I / 8;  // 16-byte pieces per h row
-    uint32_t it = 0;
-    for (int g = g_first; g < nsg; g = next_item(g), ++it) {
-      if ((int)(it % DTC_GW) != gw) continue;
-      const int bb = (int)(it % (uint32_t)NB);
-      const bool got = __all_sync(0xffffffffu, wait(&bempty[bb], ((it / (uint32_t)NB) & 1u) ^ 1u));
-      if (!got) break;
-      const int beg = r.sg_beg[g], cnt = r.sg_cnt[g];
-      uint8_t* Bt = bring + (size_t)bb * BB;
-      for (int pc = lane; pc < cnt * kc * 8; pc += 32) {
-        const int p = pc / (kc * 8), rem = pc - p * (kc * 8);
-        const int c = rem >> 3, j = rem & 7;
-        const int kv = c * 8 + j;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (kv < vecs) v = ldg16(a.h + (size_t)r.members[beg + p] * I + kv * 8);
-        *reinterpret_cast<uint4*>(Bt + c * DTC_B_CHUNK + (p >> 3) * 1024 + (p & 7) * 128 +
-                                  ((j ^ (p & 7)) << 4)) = v;
+    uint32_t its = 0;
+    bool got = true;
+    if (nst == 1) {
+      // one slice per item (inter <= 256): the item loop alone
+      for (int g = g_first; g < nsg; g = next_item(g), ++its) {
+        if ((int)(its % DTC_GW) != gw) continue;
+        const int hb = (int)(its % (uint32_t)NB);
+        got = __all_sync(0xffffffffu, wait(&bempty[hb], ((its / (uint32_t)NB) & 1u) ^ 1u));
+        if (!got) break;
+        const int beg = r.sg_beg[g], cnt = r.sg_cnt[g];
+        uint8_t* Bt = bring + (size_t)hb * BB;
+        for (int pc = lane; pc < cnt * kc * 8; pc += 32) {
+          const int p = pc / (kc * 8), rem = pc - p * (kc * 8);
+          const int c = rem >> 3, j = rem & 7;
+          const int kv = c * 8 + j;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (kv < vecs) v = ldg16(a.h + (size_t)r.members[beg + p] * I + kv * 8);
+          *reinterpret_cast<uint4*>(Bt + c * DTC_B_CHUNK + (p >> 3) * 1024 + (p & 7) * 128 +
+                                    ((j ^ (p & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[hb]);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bfull[bb]);
+    } else
+    for (int g = g_first; got && g < nsg; g = next_item(g)) {
+      const int beg = r.sg_beg[g], cnt = r.sg_cnt[g];
+      for (int sj = 0; sj < nst; ++sj, ++its) {
+        if ((int)(its % DTC_GW) != gw) continue;
+        const int hb = (int)(its % (uint32_t)NB);
+        got = __all_sync(0xffffffffu, wait(&bempty[hb], ((its / (uint32_t)NB) & 1u) ^ 1u));
+        if (!got) break;
+        const int c0 = sj * SC, nc = min(SC, kc - c0);
+        uint8_t* Bt = bring + (size_t)hb * BB;
+        for (int pc = lane; pc < cnt * nc * 8; pc += 32) {
+          const int p = pc / (nc * 8), rem = pc - p * (nc * 8);
+          const int c = rem >> 3, j = rem & 7;
+          const int kv = (c0 + c) * 8 + j;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (kv < vecs) v = ldg16(a.h + (size_t)r.members[beg + p] * I + kv * 8);
+          *reinterpret_cast<uint4*>(Bt + c * DTC_B_CHUNK + (p >> 3) * 1024 + (p & 7) * 128 +
+                                    ((j ^ (p & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[hb]);
+      }
     }
   } else {
     // ---------------- epilogue: row j = 32 * (warp % 4) + lane ------------

@@ -512,12 +512,12 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
   const int n = bn * topk;
   const int budget = dev->smem_optin - 2048;
   // Weight ring: as many K chunks in flight as fit (stages x chunks per
-  // stage), never fewer h buffers than gather warps.
+  // stage), never fewer h slices than gather warps.
   const int kc = wdb::down_tc_kc(inter);
   int stages = 0, sc = 0, nbuf = 0, smem = 0;
   for (int c : {wdb::DTC_SC, 2, 1}) {
     const int scc = std::min(c, kc);
-    for (int st = 4; st >= 2 && !smem; --st)
+    for (int st = 6; st >= 2 && !smem; --st)
       for (int nb : {8, 6, wdb::DTC_GW}) {
         const int need = wdb::down_tc_smem_bytes(st, scc, nb, inter, bn, n, E);
         if (need <= budget) {
@@ -1084,7 +1084,7 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
   if ((rc = device_info(&dev))) return rc;
   if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK ||
       (hidden + wdb::DTC_M - 1) / wdb::DTC_M > dev->sm_count)
-    return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 1024)");
+    return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 2048)");
   const wdb::TpArgs tp = make_tp_args(c);
   const int tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), std::min(64, c->max_tokens));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
