@@ -732,10 +732,19 @@ bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int int
   p.kc = 2048;  // bf16 elements: 4 KB gate and up row chunks
   const int row_bytes = inter * 2;
   p.stage_bytes = std::max(wdb::gate_up_stage_bytes(wdb::W_BF16, p.kc), ((row_bytes + 127) / 128) * 128);
-  // Down chunks: as many of the CTA's rows as fit a slot, split evenly.
+  // Down chunks: as many of the CTA's rows as fit a slot, split evenly.  With
+  // fewer than 4 rows per slot (inter > 1024) the down phase becomes a long
+  // run of tiny stages per warp: measured slower than the two kernels
+  // (inter 1536, B = 1: 112 vs 78 us), so the single launch stops there.
   const int rc_cap = std::max(1, p.stage_bytes / row_bytes);
+  if (rc_cap < 4 && p.rows_max > rc_cap) return false;
   const int nch = (p.rows_max + rc_cap - 1) / rc_cap;
   p.rc = (p.rows_max + nch - 1) / nch;
+  // Automatic choice: at most ~8 down stages per warp (slots x chunks per
+  // group / 8 warps).  Measured crossover: H 2048, inter 768, B = 4 (96
+  // stages per CTA) ran 79.8 us as one launch vs 75.9 us as two kernels,
+  // while H 4096, inter 192, B = 4 (64) gained 6 us.
+  if (max_slots < wdb::FFN_MAX_SLOTS && n * nch > 64) return false;
   p.xh_bytes = std::max(B * hidden * 2, n * inter * 2);
   p.dedup = dedup;
   const int budget = dev->smem_optin - 2048;
