@@ -172,7 +172,8 @@ __device__ __forceinline__ void dn_item(const uint8_t* __restrict__ st, const ui
   }
 }
 
-template <int FMT>
+// kRoute: routing code compiled for this launch's slot count (RouteMode).
+template <int FMT, int kRoute>
 __global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
   constexpr int WB = (FMT == W_BF16) ? 2 : 1;
   constexpr int EPV = (FMT == W_BF16) ? 8 : 16;
@@ -227,7 +228,8 @@ __global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < NCW * tile; i += blockDim.x) tiles[i] = 0.f;
-  route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);  // before the wait: re-checked
+  route_build<false, NoInit, kRoute>(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX,
+                                     a.status);  // before the wait: re-checked
 
   auto warp_total = [&](int w) {
     const int items = *r.nsg * cpg;
@@ -290,7 +292,7 @@ __global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
     // The preceding kernel rewrote topk_ids after signalling early: rebuild
     // from the settled ids; prefetched stages are drained, not used.
     if (threadIdx.x == 0) raise_status(a.status, WD_STATUS_ROUTING_CHANGED);
-    route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);
+    route_build<false, NoInit, kRoute>(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);
     if (warp < NCW) pos0 = ctrl[24 + warp];
   }
 

@@ -159,7 +159,8 @@ __device__ __forceinline__ void gu_chunk(const uint8_t* __restrict__ gs,
   }
 }
 
-template <int FMT>
+// kRoute: routing code compiled for this launch's slot count (RouteMode).
+template <int FMT, int kRoute>
 __global__ void __maxnreg__(112) moe_gate_up_kernel(const GateUpArgs a) {
   using F = GuFmt<FMT>;
   constexpr int NCW = NWARPS;
@@ -204,7 +205,8 @@ __global__ void __maxnreg__(112) moe_gate_up_kernel(const GateUpArgs a) {
       bulk_g2s_big(xs, a.x, x_bytes, xbar, l2_policy_evict_last());
     }
   }
-  route_build(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX, a.status);  // ends with __syncthreads
+  route_build<false, NoInit, kRoute>(r, a.ids, n, a.E, a.K, dedup, GROUP_MAX,
+                                     a.status);  // ends with __syncthreads
 
   const int nsg = *r.nsg;
   const int items = nsg * a.I;  // host guarantees n * I < 2^31

@@ -73,10 +73,14 @@ int device_info(DeviceInfo** out) {
     if (err == cudaSuccess)
       err = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     const void* kernels[] = {
-        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16>),
-        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3>),
-        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16>),
-        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16, wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16, wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3, wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_E4M3, wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16, wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_BF16, wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3, wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3, wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_SMALL>),
@@ -432,7 +436,9 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     cfg.stream = s;
     cfg.attrs = nullptr;
     cfg.numAttrs = 0;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_kernel<FMT>, a);
+    cudaError_t err =
+        n <= 64 ? cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_kernel<FMT, wdb::ROUTE_SMALL>, a)
+                : cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_kernel<FMT, wdb::ROUTE_LARGE>, a);
     if (err != cudaSuccess)
       return fail(WD_ERR_CUDA, std::string("gate_up launch: ") + cudaGetErrorString(err));
   }
@@ -669,7 +675,9 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, wdb::moe_down_kernel<FMT>, a);
+    cudaError_t err =
+        n <= 64 ? cudaLaunchKernelEx(&cfg, wdb::moe_down_kernel<FMT, wdb::ROUTE_SMALL>, a)
+                : cudaLaunchKernelEx(&cfg, wdb::moe_down_kernel<FMT, wdb::ROUTE_LARGE>, a);
     if (err != cudaSuccess)
       return fail(WD_ERR_CUDA, std::string("down launch: ") + cudaGetErrorString(err));
   }
