@@ -163,6 +163,78 @@ def test_config_qwen3_30b_mxfp8(wd, B):
     assert torch.equal(h, h2)
 
 
+E4M3_FINITE = np.array([b for b in range(256) if b & 0x7F != 0x7F], dtype=np.uint8)
+
+
+def mx_every_byte(rows, cols, seed, scales=(110, 127, 140)):
+    """q [1, rows, cols] holding every finite E4M3 encoding (subnormals and
+    +-0 included) at least once, block scales drawn from `scales` (dequantised
+    values stay normal in bf16, so they are exact there)."""
+    rng = np.random.default_rng(seed)
+    q = rng.choice(E4M3_FINITE, size=(1, rows, cols)).astype(np.uint8)
+    q.reshape(-1)[: E4M3_FINITE.size] = rng.permutation(E4M3_FINITE)
+    s = rng.choice(np.array(scales, dtype=np.uint8), size=(1, rows, cols // 32))
+    return torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+
+
+@pytest.mark.parametrize("B", [64, 96])
+def test_mxfp8_every_e4m3_byte_decodes_exactly(wd, B):
+    """down with one-hot h reads the weights back: y[b, n] = W[n, b] exactly,
+    for every finite E4M3 byte (the in-register decode is exact), through the
+    small (B*topk <= 64) and large routing paths."""
+    from warp_decode_b200.mxfp8 import dequantize_mxfp8
+
+    H = 256
+    q, s = mx_every_byte(H, B, 91 + B)
+    h = torch.eye(B, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(B, 1, dtype=torch.int32, device="cuda")
+    scale = torch.ones(B, 1, dtype=torch.float32, device="cuda")
+    y = wd.moe_down_3d_batched_mxfp8(h, q, s, ids, scale, B)
+    torch.cuda.synchronize()
+    want = dequantize_mxfp8(q, s)[0].t()  # [B, H]
+    assert torch.equal(want.to(torch.bfloat16).float(), want), "test weights exact in bf16"
+    bad = (y.float() != want).nonzero()
+    assert bad.numel() == 0, f"{bad.shape[0]} mismatches, first at {bad[0].tolist()}: " \
+        f"q byte 0x{int(q[0, bad[0, 1], bad[0, 0]]):02x}"
+
+
+def test_mxfp8_nan_encoding_propagates(wd):
+    """An E4M3 NaN byte (S.1111.111) makes its row's outputs NaN, as the
+    dequantised oracle does (NaN * 0 = NaN); every other row stays exact."""
+    from warp_decode_b200.mxfp8 import dequantize_mxfp8
+
+    B, H = 32, 128
+    q, s = mx_every_byte(H, B, 5)
+    q[0, 3, 17] = 0x7F
+    q[0, 40, 0] = 0xFF
+    h = torch.eye(B, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(B, 1, dtype=torch.int32, device="cuda")
+    scale = torch.ones(B, 1, dtype=torch.float32, device="cuda")
+    y = wd.moe_down_3d_batched_mxfp8(h, q, s, ids, scale, B).float()
+    torch.cuda.synchronize()
+    want = dequantize_mxfp8(q, s)[0].t()
+    nan_rows = [3, 40]
+    assert torch.isnan(y[:, nan_rows]).all()
+    keep = [n for n in range(H) if n not in nan_rows]
+    assert torch.equal(y[:, keep], want[:, keep])
+
+
+def test_mxfp8_gate_up_every_e4m3_byte(wd):
+    """gate_up with one-hot x: gate and up of token b are single weights, so h
+    = silu(W_g[n, b]) * W_u[n, b] over every finite E4M3 byte."""
+    from warp_decode_b200.mxfp8 import dequantize_mxfp8
+
+    B, I = 64, 128
+    q, s = mx_every_byte(2 * I, B, 17)
+    x = torch.eye(B, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(B, 1, dtype=torch.int32, device="cuda")
+    h = wd.moe_gate_up_3d_batched_mxfp8(x, q, s, ids)
+    torch.cuda.synchronize()
+    w = {0: dequantize_mxfp8(q[0], s[0]).cpu().numpy()}
+    h_ref = O.gate_up(host_bits(x), w, ids.cpu().numpy())
+    assert_bf16_close(host_bits(h), h_ref, what="mxfp8 gate_up, one-hot x")
+
+
 # ---------------------------------------------------------------------------
 # shapes and edge cases
 # ---------------------------------------------------------------------------

@@ -27,7 +27,7 @@ constexpr int MAX_DEDUP_E = 1024;    // experts covered by the dedup table
 constexpr int GROUP_MAX = 8;         // slots per group (register accumulators)
 constexpr int NWARPS = 8;            // compute warps per CTA (both kernels)
 #ifndef WD_GU_DEPTH
-#define WD_GU_DEPTH 2
+#define WD_GU_DEPTH 8
 #endif
 constexpr int GU_DEPTH_MAX = WD_GU_DEPTH;  // gate_up ring slots per consumer warp
 
@@ -199,6 +199,53 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t s) {
   if (s == 0u) return __uint_as_float(0x00400000u);  // 2^-127 (fp32 subnormal)
   if (s == 255u) return __uint_as_float(0x7fc00000u);
   return __uint_as_float(s << 23);
+}
+
+// The fixed factor of e4m3x16_to_bf16: decoded values are E4M3 x 2^-120.
+constexpr float E4M3_BF16_UNSCALE = 0x1p120f;
+
+// Sixteen OCP E4M3 bytes -> sixteen bf16 values in eight packed pairs (byte
+// 2j in the low half of p[j]), exact, every value carrying the fixed factor
+// 2^-120.  Per byte s.eeee.mmm the bf16 pattern is s at bit 15 and eeee.mmm
+// at bits 10..4: an exponent field of e (bias 127 instead of 7, hence the
+// 2^-120) with the three mantissa bits on top of bf16's seven, so E4M3
+// subnormals (e = 0) land on bf16 subnormals of the same scaled value.  The
+// sign-replicating selectors of prmt build [sign x 8 | byte] per 16-bit lane,
+// then a shift by 4 and one mask keep sign and magnitude: three integer
+// operations per pair, no conversion instructions.  Returns true if some byte
+// is an E4M3 NaN (magnitude 0x7f, which would decode to a finite 480 x
+// 2^-120): the caller then makes its block scale NaN.  NaN test: x = ~byte &
+// 0x7f is 0 exactly for magnitude 0x7f; (x - 1) sets bit 7 of a byte only
+// where some byte of the word is 0 (the zero-byte test of Mycroft, 1987).
+__device__ __forceinline__ bool e4m3x16_to_bf16(const uint4& v, uint32_t (&p)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t zero_bytes = 0u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t a, b;
+    asm("prmt.b32 %0, %1, 0, 0x9180;" : "=r"(a) : "r"(w[q]));
+    asm("prmt.b32 %0, %1, 0, 0xB3A2;" : "=r"(b) : "r"(w[q]));
+    p[2 * q] = (a << 4) & 0x87f087f0u;
+    p[2 * q + 1] = (b << 4) & 0x87f087f0u;
+    zero_bytes |= (~w[q] & 0x7f7f7f7fu) - 0x01010101u;
+  }
+  return (zero_bytes & 0x80808080u) != 0u;
+}
+
+// acc0 += (x[0..7] . w[0..7]) part, acc1 += (x[8..15] . w[8..15]) part, for
+// 16 bf16 activations (two 16-byte vectors) against 16 decoded E4M3 weights:
+// the same mixed-precision FMA as bf16 weights, on the 2^-120-scaled values.
+__device__ __forceinline__ void dot16_e4m3(float& a0, float& a1, const uint4& xa, const uint4& xb,
+                                           const uint32_t (&p)[8]) {
+  dot8_bf16(a0, a1, xa, make_uint4(p[0], p[1], p[2], p[3]));
+  dot8_bf16(a0, a1, xb, make_uint4(p[4], p[5], p[6], p[7]));
+}
+
+// One lane's 16-element part of an MX block into the accumulator: the scaled
+// sum times 2^120 (exact) times the block scale, or NaN for a NaN byte.
+__device__ __forceinline__ float mx_block_fma(float part, uint32_t s, bool nan_byte, float acc) {
+  const float sc = nan_byte ? __uint_as_float(0x7fc00000u) : ue8m0_to_f32(s);
+  return fmaf(part * E4M3_BF16_UNSCALE, sc, acc);
 }
 
 // ---------------------------------------------------------------------------

@@ -80,24 +80,20 @@ __device__ __forceinline__ void dn_row(const uint8_t* __restrict__ wrow, const u
         if (m < cnt) dot8_bf16(acc[m], acc2[m], act16(hr[m] + v * 8, hsm), wv);
     }
   } else {
+    // E4M3: decoded to exact bf16 patterns (scaled by 2^-120), the bf16 FMA,
+    // then 2^120 x the block scale once per 16-element vector.
 #pragma unroll 2
     for (int v = lj; v < nvec; v += lpr) {
-      float wf[16];
-      unpack_e4m3x16(lds16(wrow + v * 16), wf);
-      const float sc = ue8m0_to_f32(srow[v >> 1]);
+      uint32_t wb[8];
+      const bool nan_byte = e4m3x16_to_bf16(lds16(wrow + v * 16), wb);
+      const uint32_t s = srow[v >> 1];
 #pragma unroll
       for (int m = 0; m < MAXM; ++m) {
         if (m < cnt) {
-          float ha[8], hb[8];
-          unpack_bf16x8(act16(hr[m] + v * 16, hsm), ha);
-          unpack_bf16x8(act16(hr[m] + v * 16 + 8, hsm), hb);
-          float s = 0.f, s2 = 0.f;
-#pragma unroll
-          for (int t = 0; t < 8; ++t) s = fmaf(ha[t], wf[t], s);
-#pragma unroll
-          for (int t = 0; t < 8; ++t) s2 = fmaf(hb[t], wf[8 + t], s2);
-          acc[m] = fmaf(s, sc, acc[m]);
-          acc2[m] = fmaf(s2, sc, acc2[m]);
+          float p = 0.f, p2 = 0.f;
+          dot16_e4m3(p, p2, act16(hr[m] + v * 16, hsm), act16(hr[m] + v * 16 + 8, hsm), wb);
+          acc[m] = mx_block_fma(p, s, nan_byte, acc[m]);
+          acc2[m] = mx_block_fma(p2, s, nan_byte, acc2[m]);
         }
       }
     }
@@ -174,7 +170,7 @@ __device__ __forceinline__ void dn_item(const uint8_t* __restrict__ st, const ui
 
 // kRoute: routing code compiled for this launch's slot count (RouteMode).
 template <int FMT, int kRoute>
-__global__ void __maxnreg__(112) moe_down_kernel(const DownArgs a) {
+__global__ void __maxnreg__(FMT == W_E4M3 ? 96 : 112) moe_down_kernel(const DownArgs a) {
   constexpr int WB = (FMT == W_BF16) ? 2 : 1;
   constexpr int EPV = (FMT == W_BF16) ? 8 : 16;
   constexpr int NCW = NWARPS;

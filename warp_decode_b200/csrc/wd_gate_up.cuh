@@ -14,7 +14,7 @@
 //  * Every consumer warp owns `depth` ring slots.  Lane w of the producer warp
 //    feeds consumer warp w: it polls that warp's "empty" mbarriers without
 //    blocking and issues cp.async.bulk copies of the gate and up row chunks
-//    (4 KB each) into the freed slot, completing the slot's "full" mbarrier
+//    (up to 4 KB each) into the freed slot, completing the slot's "full" mbarrier
 //    by byte count.  The 8 lanes issue in parallel, so copy issue never sits
 //    on a consumer's critical path, and a slot is only ever consumed, in
 //    order, by one warp.
@@ -79,21 +79,6 @@ __host__ inline int gate_up_smem_bytes(int depth, int stage_bytes, int x_bytes, 
 
 __device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
 
-__device__ __forceinline__ void unpack_e4m3x16(const uint4& v, float (&f)[16]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(
-        static_cast<__nv_fp8x2_storage_t>(w[q] & 0xffffu), __NV_E4M3);
-    const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(
-        static_cast<__nv_fp8x2_storage_t>(w[q] >> 16), __NV_E4M3);
-    const float2 a = __half22float2(__half2(lo));
-    const float2 b = __half22float2(__half2(hi));
-    f[4 * q + 0] = a.x; f[4 * q + 1] = a.y;
-    f[4 * q + 2] = b.x; f[4 * q + 3] = b.y;
-  }
-}
-
 // 16-byte activation vector: shared-memory tile or global memory.
 __device__ __forceinline__ uint4 act16(const __nv_bfloat16* p, bool smem) {
   return smem ? lds16(p) : ldg16(p);
@@ -125,43 +110,36 @@ __device__ __forceinline__ void gu_chunk(const uint8_t* __restrict__ gs,
       }
     }
   } else {
-#pragma unroll 2
+    // E4M3: decoded to exact bf16 patterns (scaled by 2^-120), the bf16 FMA,
+    // then 2^120 x the block scale once per lane and block.  Not unrolled:
+    // registers stay within the two-CTAs-per-SM budget.
+#pragma unroll 1
     for (int k = lane * 16; k < klen; k += 512) {
-      float gf[16], uf[16];
-      unpack_e4m3x16(lds16(gs + k), gf);
-      unpack_e4m3x16(lds16(us + k), uf);
-      const float sg = ue8m0_to_f32(gsc[k >> 5]);
-      const float su = ue8m0_to_f32(usc[k >> 5]);
+      uint32_t gw[8], uw[8];
+      const bool gnan = e4m3x16_to_bf16(lds16(gs + k), gw);
+      const bool unan = e4m3x16_to_bf16(lds16(us + k), uw);
+      const uint32_t sg = gsc[k >> 5];
+      const uint32_t su = usc[k >> 5];
 #pragma unroll
       for (int m = 0; m < MAXM; ++m) {
         if (m < cnt) {
-          float xa[8], xb[8];
-          unpack_bf16x8(act16(xr[m] + k, xsm), xa);
-          unpack_bf16x8(act16(xr[m] + k + 8, xsm), xb);
-          float g = 0.f, u = 0.f, g2 = 0.f, u2 = 0.f;
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            g = fmaf(xa[t], gf[t], g);
-            u = fmaf(xa[t], uf[t], u);
-          }
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            g2 = fmaf(xb[t], gf[8 + t], g2);
-            u2 = fmaf(xb[t], uf[8 + t], u2);
-          }
-          ag[m] = fmaf(g, sg, ag[m]);
-          ag2[m] = fmaf(g2, sg, ag2[m]);
-          au[m] = fmaf(u, su, au[m]);
-          au2[m] = fmaf(u2, su, au2[m]);
+          const uint4 xa = act16(xr[m] + k, xsm);
+          const uint4 xb = act16(xr[m] + k + 8, xsm);
+          float g = 0.f, g2 = 0.f, u = 0.f, u2 = 0.f;
+          dot16_e4m3(g, g2, xa, xb, gw);
+          dot16_e4m3(u, u2, xa, xb, uw);
+          ag[m] = mx_block_fma(g, sg, gnan, ag[m]);
+          ag2[m] = mx_block_fma(g2, sg, gnan, ag2[m]);
+          au[m] = mx_block_fma(u, su, unan, au[m]);
+          au2[m] = mx_block_fma(u2, su, unan, au2[m]);
         }
       }
     }
   }
 }
 
-// kRoute: routing code compiled for this launch's slot count (RouteMode).
 template <int FMT, int kRoute>
-__global__ void __maxnreg__(112) moe_gate_up_kernel(const GateUpArgs a) {
+__global__ void __maxnreg__(FMT == W_E4M3 ? 96 : 112) moe_gate_up_kernel(const GateUpArgs a) {
   using F = GuFmt<FMT>;
   constexpr int NCW = NWARPS;
 

@@ -51,6 +51,8 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sm_count = 0;
   int smem_optin = 0;
+  int smem_per_sm = 0;      // shared memory of one SM
+  int smem_reserved = 0;    // shared memory the runtime reserves per CTA
   unsigned long long* ffn_sync = nullptr;  // library-owned grid-barrier counter (g_wd_ffn_sync)
   unsigned char* noalloc_scratch = nullptr;  // g_wd_noalloc_scratch, set on first use
   bool ready = false;
@@ -72,6 +74,10 @@ int device_info(DeviceInfo** out) {
     err = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (err == cudaSuccess)
       err = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (err == cudaSuccess)
+      err = cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (err == cudaSuccess)
+      err = cudaDeviceGetAttribute(&d.smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
     const void* kernels[] = {
         reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16, wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_kernel<wdb::W_BF16, wdb::ROUTE_LARGE>),
@@ -393,27 +399,42 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
       continue;
     }
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
-    // Ring: 8 warps x `depth` slots of (gate, up) row chunks of 4 KB each; x
-    // staged in shared memory if it fits in 128 KB.  Preference order: a
-    // deep ring (at B=1 a CTA's whole share, ~170 KB, is then requested at
-    // once: one copy latency instead of two), then x staged, then 2 KB
-    // chunks, then x read from L2.
+    // Ring: 8 warps x `depth` slots of (gate, up) row chunks of up to 4 KB
+    // each, a chunk never longer than the row (hidden < 4 KB of weights gives
+    // smaller slots rather than half-empty ones); x staged in shared memory
+    // if it fits in 128 KB.  Preference order: x staged with the deepest ring
+    // that fits (up to GU_DEPTH_MAX slots per warp: the bytes in flight per
+    // SM set the rate of this latency-bound stream; at B = 1 a CTA's whole
+    // share is then requested at once), then 2 KB chunks, then x from L2.
     const long long x_bytes = (long long)bn * hidden * 2;
     const bool x_fits = x_bytes <= 128 * 1024;
-    const int budget = dev->smem_optin - 2048;
-    struct Choice { int depth, kc; bool x_smem; };
-    const Choice choices[] = {{wdb::GU_DEPTH_MAX, 4096 / WB, x_fits}, {2, 4096 / WB, x_fits},
-                              {2, 2048 / WB, x_fits}, {2, 2048 / WB, false}};
+    const int kc_full = std::min(4096 / WB, ((hidden + 31) / 32) * 32);
+    struct Choice { int kc; bool x_smem; };
+    const Choice choices[] = {{kc_full, x_fits}, {std::min(kc_full, 2048 / WB), x_fits},
+                              {std::min(kc_full, 2048 / WB), false}};
     int kc = 0, depth = 0, smem = 0;
     bool x_smem = false;
-    for (const Choice& c : choices) {
-      const int need = wdb::gate_up_smem_bytes(c.depth, wdb::gate_up_stage_bytes(FMT, c.kc),
-                                               c.x_smem ? (int)x_bytes : 0, n, E, dedup);
-      if (need <= budget) {
-        kc = c.kc; depth = c.depth; x_smem = c.x_smem; smem = need;
-        break;
+    auto plan = [&](int budget) {
+      for (const Choice& c : choices) {
+        for (int d = wdb::GU_DEPTH_MAX; d >= 2 && !smem; --d) {
+          const int need = wdb::gate_up_smem_bytes(d, wdb::gate_up_stage_bytes(FMT, c.kc),
+                                                   c.x_smem ? (int)x_bytes : 0, n, E, dedup);
+          if (need <= budget) {
+            kc = c.kc; depth = d; x_smem = c.x_smem; smem = need;
+          }
+        }
+        if (smem) return;
       }
+    };
+    // MXFP8: two CTAs per SM when a plan fits half of the SM's shared memory
+    // (the E4M3 decode makes this stream issue-latency bound; twice the warps
+    // per scheduler hide it).  bf16 and larger plans: one CTA per SM.
+    int ctas_per_sm = 1;
+    if (FMT == wdb::W_E4M3) {
+      plan(dev->smem_per_sm / 2 - dev->smem_reserved - 1024);
+      if (smem) ctas_per_sm = 2;
     }
+    if (!smem) plan(dev->smem_optin - 2048);
     if (!smem) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
     wdb::GateUpArgs a;
     a.x = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
@@ -430,7 +451,7 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     a.x_smem = x_smem ? 1 : 0;
     const long long work = (long long)n * inter;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+    cfg.gridDim = dim3((unsigned)std::min<long long>((long long)ctas_per_sm * dev->sm_count, work));
     cfg.blockDim = dim3(wdb::GU_THREADS);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
@@ -606,22 +627,45 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
 
   constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
   constexpr int EPV = FMT == wdb::W_BF16 ? 8 : 16;
-  const int grid = std::max(1, std::min(dev->sm_count, hidden / 4));
-  const int rows_max = (hidden + grid - 1) / grid;
   const int row_bytes = inter * WB;
-  // Item = chunk of >= 4 KB of contiguous rows (smaller bulk copies do not
-  // saturate HBM), chunks of one CTA's block as even as that allows.
-  const int rc_min = std::min(rows_max, std::max(1, (4096 + row_bytes - 1) / row_bytes));
-  const int nch = std::max(1, rows_max / rc_min);
-  const int rows_chunk = (rows_max + nch - 1) / nch;
   const int nvec = inter / EPV;
   const int lpr = nvec <= 32 ? 8 : (nvec <= 64 ? 16 : 32);
-  int stage_bytes = rows_chunk * row_bytes + wdb::down_scale_area<FMT>(rows_chunk, inter);
-  stage_bytes = ((stage_bytes + 127) / 128) * 128;
-  const int depth = std::min(4, std::max(2, (96 * 1024) / (wdb::NWARPS * stage_bytes)));
-  // Tokens per launch: routing capacity and the 8 per-warp FP32 tiles.
-  int tb = std::max(1, wdb::MAX_SLOTS / topk);
-  tb = std::min(tb, std::max(1, (64 * 1024) / (4 * wdb::NWARPS * rows_max)));
+  int grid = 0, rows_max = 0, rows_chunk = 0, stage_bytes = 0, depth = 0, tb = 0;
+  // Geometry for a grid of g CTAs, each owning a block of rows_max rows.
+  auto geometry = [&](int g) {
+    grid = g;
+    rows_max = (hidden + grid - 1) / grid;
+    // Item = chunk of >= 4 KB of contiguous rows (smaller bulk copies do not
+    // saturate HBM), chunks of one CTA's block as even as that allows.
+    const int rc_min = std::min(rows_max, std::max(1, (4096 + row_bytes - 1) / row_bytes));
+    const int nch = std::max(1, rows_max / rc_min);
+    rows_chunk = (rows_max + nch - 1) / nch;
+    stage_bytes = rows_chunk * row_bytes + wdb::down_scale_area<FMT>(rows_chunk, inter);
+    stage_bytes = ((stage_bytes + 127) / 128) * 128;
+    depth = std::min(4, std::max(2, (96 * 1024) / (wdb::NWARPS * stage_bytes)));
+    // Tokens per launch: routing capacity and the 8 per-warp FP32 tiles.
+    tb = std::max(1, wdb::MAX_SLOTS / topk);
+    tb = std::min(tb, std::max(1, (64 * 1024) / (4 * wdb::NWARPS * rows_max)));
+  };
+  auto smem_need = [&](int bn, bool h_smem) {
+    const int n = bn * topk;
+    const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
+    return wdb::down_smem_bytes(depth, stage_bytes, h_smem ? n * inter * 2 : 0, bn, rows_max, n,
+                                E, dedup);
+  };
+  // MXFP8: two CTAs per SM when every launch of the call fits half of the
+  // SM's shared memory (the E4M3 decode makes this stream issue-latency
+  // bound; twice the warps per scheduler hide it).  bf16: one CTA per SM.
+  int budget = dev->smem_optin - 2048;
+  if (FMT == wdb::W_E4M3 && hidden / 4 >= 2 * dev->sm_count) {
+    geometry(2 * dev->sm_count);
+    const int half = dev->smem_per_sm / 2 - dev->smem_reserved - 1024;
+    if (smem_need(std::min(tb, B), false) <= half)
+      budget = half;
+    else
+      grid = 0;
+  }
+  if (!grid) geometry(std::max(1, std::min(dev->sm_count, hidden / 4)));
   const bool tc = FMT == wdb::W_BF16 && down_tc_applies(B, E, hidden, inter, dev->sm_count);
   if (tc) tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), 64);
 
@@ -644,13 +688,9 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
     const bool dedup = bn > 1 && E <= wdb::MAX_DEDUP_E;
     const long long h_bytes = (long long)n * inter * 2;
     bool h_smem = h_bytes <= 64 * 1024;
-    auto need = [&]() {
-      return wdb::down_smem_bytes(depth, stage_bytes, h_smem ? (int)h_bytes : 0, bn, rows_max, n,
-                                  E, dedup);
-    };
-    const int budget = dev->smem_optin - 2048;
-    if (need() > budget) h_smem = false;
-    if (need() > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+    if (smem_need(bn, h_smem) > budget) h_smem = false;
+    const int smem = smem_need(bn, h_smem);
+    if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
     wdb::DownArgs a;
     a.h = reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter;
     a.w = w;
@@ -671,7 +711,7 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(wdb::DN_THREADS);
-    cfg.dynamicSmemBytes = (size_t)need();
+    cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
