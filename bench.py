@@ -19,6 +19,11 @@ slice of an inter = 192*N FFN (at N = 8 the full-width Qwen3-235B FFN split
 TP=8); the call ends with one NCCL all-reduce of the FP32 partial [B, 4096]
 output, then the bf16 cast.  Per-GPU work is fixed: "scaling": "weak".
 
+--workload selects another BASELINE configuration at the same method:
+qwen3_235b_full (inter 1536 split over the N GPUs: strong scaling), dsv3_tp8
+(hidden 7168, 256 experts, Zipf routing), qwen3_30b_mxfp8 (MXFP8 weights,
+one GPU).  The default is the headline workload above.
+
 --impl reference times the reference's PyTorch path (gather + bf16 bmm,
 tests/test_gate_up_correctness.py:19-43 / tests/test_down_correctness.py:14-35)
 on the host cores, via the CPU port in oracle/torch_port.py.
@@ -56,7 +61,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--batches", default=",".join(map(str, SWEEP)))
+    p.add_argument("--workload", default=WORKLOAD,
+                   choices=["qwen3_235b_tp8", "qwen3_235b_full", "dsv3_tp8", "qwen3_30b_mxfp8"],
+                   help="BASELINE configuration (default: the headline TP=8 shard)")
+    p.add_argument("--batches", default=None, help="comma-separated B values (default: the workload's)")
     p.add_argument("--hot-iters", type=int, default=200, help="graph replays for the L2-warm numbers")
     p.add_argument("--kernel-reps", type=int, default=30, help="cold reps per kernel measurement")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
@@ -193,11 +201,44 @@ def run_ours(args, rank, local_rank, world):
     dev = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    batches = [int(b) for b in args.batches.split(",")]
-    cfg = W.CONFIGS[WORKLOAD]
-    H, I, E, K = cfg.hidden, cfg.inter, cfg.E, cfg.topk
+    cfg = W.CONFIGS[args.workload]
+    batches = [int(b) for b in args.batches.split(",")] if args.batches else list(cfg.batches)
+    mx = cfg.weights == "mxfp8"
+    if mx and world > 1:
+        raise SystemExit("bench.py: the MXFP8 workload runs on one GPU")
+    # qwen3_235b_full: the fixed full-width FFN split over the ranks (strong
+    # scaling); the shard workloads: every rank one shard-sized slice (weak).
+    strong = args.workload == "qwen3_235b_full"
+    H, E, K = cfg.hidden, cfg.E, cfg.topk
+    I = cfg.inter_full // world if strong else cfg.inter
 
     w_gu, w_dn = W.make_device_weights(H, I, E, args.seed + 7919 * rank, device=dev)
+    if mx:
+        from warp_decode_b200.mxfp8 import quantize_mxfp8
+
+        gq, gs = quantize_mxfp8(w_gu)
+        dq, ds = quantize_mxfp8(w_dn)
+        del w_gu, w_dn
+        torch.cuda.empty_cache()
+
+        def gate_up(x, ids):
+            return wd.moe_gate_up_3d_batched_mxfp8(x, gq, gs, ids)
+
+        def down(h, ids, sc, B):
+            return wd.moe_down_3d_batched_mxfp8(h, dq, ds, ids, sc, B)
+
+        def ffn(x, ids, sc):
+            return down(gate_up(x, ids), ids, sc, x.shape[0])
+    else:
+        def gate_up(x, ids):
+            return wd.moe_gate_up_3d_batched(x, w_gu, ids)
+
+        def down(h, ids, sc, B):
+            return wd.moe_down_3d_batched(h, w_dn, ids, sc, B)
+
+        def ffn(x, ids, sc):
+            # one call: single cooperative launch where it applies, else the two kernels
+            return wd.moe_ffn_3d_batched(x, w_gu, w_dn, ids, sc)
     flush = L2Flush(dev)
     stream = torch.cuda.Stream(device=dev)
 
@@ -210,7 +251,7 @@ def run_ours(args, rank, local_rank, world):
         c.B = B
         c.x, c.ids, c.scale = W.make_device_activations(B, H, E, K, cfg.routing, args.seed + B, device=dev)
         c.U = W.unique_experts(c.ids.cpu().numpy())
-        c.bytes = W.algorithmic_bytes(c.U, B, H, I, K)
+        c.bytes = W.algorithmic_bytes(c.U, B, H, I, K, cfg.weights)
         cases[B] = c
 
     fused = None
@@ -221,8 +262,7 @@ def run_ours(args, rank, local_rank, world):
 
     def e2e_call(c):
         if world == 1:
-            # one call: single cooperative launch for B*topk <= 64, else the two kernels
-            return wd.moe_ffn_3d_batched(c.x, w_gu, w_dn, c.ids, c.scale)
+            return ffn(c.x, c.ids, c.scale)
         if fused is not None and fused.applies(c.B):
             # one launch (FFN + exchange) for B*topk <= 32, else gate_up + down
             return fused.ffn(c.x, w_gu, w_dn, c.ids, c.scale)
@@ -232,27 +272,25 @@ def run_ours(args, rank, local_rank, world):
         return part.to(torch.bfloat16)
 
     def capture(fn):
+        """CUDA graph of one call, and how many of the library's kernels it holds."""
         with torch.cuda.stream(stream):
             for _ in range(3):
                 fn()
         stream.synchronize()
         g = torch.cuda.CUDAGraph()
+        n0 = wd.launch_count()
         with torch.cuda.graph(g, stream=stream):
             out = fn()
-        return g, out
+        return g, out, wd.launch_count() - n0
 
+    launches = {}
     for c in cases.values():
-        c.g_e2e, c.y = capture(lambda c=c: e2e_call(c))
-        c.g_gu, c.h = capture(lambda c=c: wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids))
-        c.g_dn, _ = capture(lambda c=c: wd.moe_down_3d_batched(c.h, w_dn, c.ids, c.scale, c.B))
+        c.g_e2e, c.y, launches[c.B] = capture(lambda c=c: e2e_call(c))
+        c.g_gu, c.h, _ = capture(lambda c=c: gate_up(c.x, c.ids))
+        c.g_dn, _, _ = capture(lambda c=c: down(c.h, c.ids, c.scale, c.B))
         c.g_split = None
-        if world == 1:
-            c.g_split, _ = capture(lambda c=c: wd.moe_down_3d_batched(
-                wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids), w_dn, c.ids, c.scale, c.B))
-    # kernels per e2e call: the single-launch FFN is the automatic choice for
-    # B*topk <= 32 at this workload's shapes, else gate_up + down
-    launches = {B: (1 if B * K <= 32 and (world == 1 or (fused is not None and fused.applies(B)))
-                    else 2) for B in batches}
+        if world == 1 and not mx:
+            c.g_split, _, _ = capture(lambda c=c: down(gate_up(c.x, c.ids), c.ids, c.scale, c.B))
     torch.cuda.synchronize()
 
     def barrier():
@@ -340,12 +378,13 @@ def run_ours(args, rank, local_rank, world):
                 "e2e_frac": round(c.bytes["e2e"] / (per_b_us[B] * 1e-6) / 1e9 / peak_gbs, 3),
                 "gate_up_frac": round(c.bytes["gate_up"] / (t_gu * 1e-6) / 1e9 / peak_gbs, 3),
                 "down_frac": round(c.bytes["down"] / (t_dn * 1e-6) / 1e9 / peak_gbs, 3),
-                "published_h20_hot_e2e_us": PUBLISHED_H20_E2E_US.get(B),
+                "published_h20_hot_e2e_us": (PUBLISHED_H20_E2E_US.get(B)
+                                             if args.workload == WORKLOAD else None),
             })
         achieved = gu_bytes / (gu_time * 1e-6) / 1e9
         traffic = None
         tpath = ROOT / "profiles" / "gate_up_dram_traffic.json"
-        if tpath.exists():
+        if tpath.exists() and args.workload == WORKLOAD:
             try:
                 t = json.loads(tpath.read_text())
                 per = [t["per_batch"][str(B)] for B in batches if str(B) in t["per_batch"]]
@@ -353,7 +392,9 @@ def run_ours(args, rank, local_rank, world):
                     traffic = sum(per) / nB
             except Exception:
                 traffic = None
-        roofline = {"bound": "hbm", "kernel": "gate_up (moe_gate_up_kernel B<16, moe_gate_up_tc_kernel B>=16)", "achieved": round(achieved, 1),
+        kname = ("gate_up (moe_gate_up_kernel<e4m3>, MXFP8 weights)" if mx else
+                 "gate_up (moe_gate_up_kernel B<16, moe_gate_up_tc_kernel B>=16)")
+        roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                     "peak": peak_gbs, "peak_kind": peak_kind, "unit": "GB/s",
                     "frac": round(achieved / peak_gbs, 4),
                     "alg_bytes_per_launch": gu_bytes / nB, "traffic": traffic,
@@ -388,7 +429,7 @@ def run_ours(args, rank, local_rank, world):
                 a.record(cur)
                 dbuf.copy_(host, non_blocking=True)
                 if world == 1:
-                    y = wd.moe_ffn_3d_batched(xd, w_gu, w_dn, idd, scd)
+                    y = ffn(xd, idd, scd)
                 elif fused is not None and fused.applies(B):
                     y = fused.ffn(xd, w_gu, w_dn, idd, scd)
                 else:
@@ -409,6 +450,8 @@ def run_ours(args, rank, local_rank, world):
         e2e = {"value": round(float(e2e_total.item()) * 1000.0 / (len(e2e_ts) * nB), 3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "method": ("eager torch API (moe_ffn_3d_batched) per call"
+                          if world == 1 and not mx else
+                          "eager torch API (moe_gate_up_3d_batched_mxfp8 + moe_down_3d_batched_mxfp8) per call"
                           if world == 1 else
                           "eager torch API (FusedAllReduce.ffn, or moe_gate_up_3d_batched + "
                           "moe_down_3d_batched_partial + all_reduce above the fused size) per call") +
@@ -419,6 +462,8 @@ def run_ours(args, rank, local_rank, world):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_timing(batches, H, I, E, K, cfg.routing, budget_s=args.cpu_seconds,
                                    steps=None)
+        if mx:
+            cpu["sample"] += " (bf16 weights: the reference has no MXFP8 path)"
 
     clocks_all = [clocks]
     if world > 1:
@@ -430,13 +475,17 @@ def run_ours(args, rank, local_rank, world):
         clock_rec = {"sm_mhz": statistics.median(mhz) if mhz else None,
                      "sm_max_mhz": clocks_all[0].get("sm_max_mhz") if clocks_all[0] else None,
                      "reasons": reasons, "samples": sum(c.get("samples", 0) for c in clocks_all if c)}
+        wname = workload_name(args.workload, cfg, world)
+        routing = {"uniform": "uniform distinct", "zipf": "Zipf(1.1) distinct"}.get(cfg.routing, cfg.routing)
         line = {
             "metric": METRIC, "value": round(value_us, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded; x~N(0,1), W~N(0,fan_in^-1/2), uniform distinct top-8, softmax weights)",
-            "config": {"workload": WORKLOAD if world == 1 else f"qwen3_235b_inter{I * world}_tp{world}",
-                       "hidden": H, "inter_per_gpu": I, "inter_total": I * world, "experts": E,
+            "higher_is_better": False, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "e4m3 weights (MXFP8, ue8m0 per 32) x bf16 activations, fp32 accumulate" if mx else "bf16",
+            "data": f"synthetic (seeded; x~N(0,1), W~N(0,fan_in^-1/2), {routing} top-{K}, softmax weights"
+                    + (", W quantised to MXFP8 on the device)" if mx else ")"),
+            "config": {"workload": wname,
+                       "hidden": H, "inter_per_gpu": I, "inter_total": cfg.inter_full if strong else I * world, "experts": E,
                        "topk": K, "batches": batches, "global_batch": batches,
                        "parallelism": "single GPU" if world == 1 else (
                            f"tp{world} over inter + all-reduce fused into the kernels (NVLink peer stores; "
@@ -530,15 +579,27 @@ def cpu_reference_timing(batches, H, I, E, K, routing, budget_s=12.0, steps=None
             "step_ms": step_ms}
 
 
+def workload_name(workload, cfg, world):
+    """config.workload of the JSON line for `workload` run on `world` GPUs."""
+    if world == 1:
+        return workload
+    if workload == "qwen3_235b_full":
+        return f"{workload}_tp{world}"
+    if workload == WORKLOAD:
+        return f"qwen3_235b_inter{cfg.inter * world}_tp{world}"
+    return f"{workload}_inter{cfg.inter * world}_tp{world}"
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's PyTorch path on the host cores (rank 0 only)."""
     if rank != 0:
         return 0
     from warp_decode_b200 import workloads as W
 
-    batches = [int(b) for b in args.batches.split(",")]
-    cfg = W.CONFIGS[WORKLOAD]
-    I_total = cfg.inter * world  # the reference has no tensor parallelism: full width on CPU
+    cfg = W.CONFIGS[args.workload]
+    batches = [int(b) for b in args.batches.split(",")] if args.batches else list(cfg.batches)
+    # the reference has no tensor parallelism: the whole FFN of the N-GPU run on CPU
+    I_total = cfg.inter_full if args.workload == "qwen3_235b_full" else cfg.inter * world
     budget = min(150.0, 2.0 * (args.steps + args.warmup))
     r = cpu_reference_timing(batches, cfg.hidden, I_total, cfg.E, cfg.topk, cfg.routing,
                              budget_s=budget, steps=args.steps, warmup=args.warmup)
@@ -546,8 +607,9 @@ def run_reference(args, rank, world):
     line = {
         "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD if world == 1 else f"qwen3_235b_inter{I_total}_tp{world}",
+        "scaling": "strong" if args.workload == "qwen3_235b_full" else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload_name(args.workload, cfg, world),
                    "hidden": cfg.hidden, "inter_total": I_total, "experts": cfg.E, "topk": cfg.topk,
                    "batches": batches, "parallelism": "CPU, all host threads"},
         "impl": "reference",

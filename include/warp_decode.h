@@ -136,6 +136,16 @@ WD_API int wd_moe_down_3d_batched_mxfp8(const void* h, const uint8_t* w_q, const
 WD_API int wd_status_read(uint32_t* value, int clear);
 
 /*
+ * Number of kernels this library has enqueued so far in this process, over
+ * all devices and threads.  Counted on the host when a launch is accepted, so
+ * a CUDA-graph capture counts the launches it records and a replay counts
+ * none; calls rejected by argument checks count none.  No counterpart in the
+ * reference (a benchmark reads it around one captured call to report how
+ * many kernels the call runs).
+ */
+WD_API unsigned long long wd_launch_count(void);
+
+/*
  * Choose the kernel behind wd_moe_gate_up_3d_batched (bf16 weights), for all
  * later calls in this process: 0 = automatic (tcgen05 tensor-core kernel from
  * 16 tokens per call, SIMT kernel below), 1 = SIMT kernel only, 2 = tensor-

@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 19, names
+    assert len(names) == 20, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -77,6 +77,14 @@ def test_version_and_error_strings():
     assert L.wd_version() >= 100
     assert L.wd_error_string(capi.WD_ERR_SHAPE) == b"invalid shape"
     assert L.wd_error_string(99) == b"unknown error"
+
+
+def test_rejected_calls_launch_nothing():
+    L = capi.lib()
+    before = L.wd_launch_count()
+    assert capi.gate_up(0x1000, 0x2000, 0x3000, 0x4000, -1, 4, 2, 256, 8) == capi.WD_ERR_SHAPE
+    assert capi.gate_up(0, 0x2000, 0x3000, 0x4000, 2, 4, 2, 256, 8) == capi.WD_ERR_NULL_POINTER
+    assert L.wd_launch_count() == before
 
 
 @pytest.mark.parametrize("args,code,msg", [

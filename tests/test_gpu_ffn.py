@@ -203,3 +203,33 @@ def test_graph_replay_and_determinism(wd):
     assert wd.status(True, torch.cuda.current_device()) == 0
     for o in eager[1:] + outs:
         assert np.array_equal(o, eager[0])
+
+
+def test_launch_count(wd):
+    """wd_launch_count: one launch per call on the single-launch path, two when
+    the FFN runs as gate_up + down, and none for a graph replay."""
+    c = W.CONFIGS["qwen3_235b_tp8"]
+    wgu, wdn = weights(c.hidden, c.inter, c.E, 41)
+    x, ids, scale = W.make_device_activations(2, c.hidden, c.E, c.topk, c.routing, 8700)
+    for path, n in ((capi.FFN_FUSED, 1), (capi.FFN_SPLIT, 2)):
+        capi.set_ffn_path(path)
+        try:
+            n0 = wd.launch_count()
+            wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale)
+            assert wd.launch_count() - n0 == n
+        finally:
+            capi.set_ffn_path(capi.FFN_AUTO)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    n0 = wd.launch_count()
+    with torch.cuda.graph(g, stream=s):
+        wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale)
+    recorded = wd.launch_count() - n0
+    g.replay()
+    torch.cuda.synchronize()
+    assert recorded == 1 and wd.launch_count() - n0 == 1
+    del g
+    assert wd.status(True, torch.cuda.current_device()) == 0

@@ -36,6 +36,7 @@ _SIGS = {
     "wd_moe_gate_up_3d_batched_mxfp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "wd_moe_down_3d_batched_mxfp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "wd_status_read": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "wd_launch_count": (ctypes.c_ulonglong, []),
     "wd_set_gate_up_path": (_I, [_I]),
     "wd_set_down_path": (_I, [_I]),
     "wd_tp_comm_create": (_I, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p), _P]),

@@ -223,6 +223,8 @@ int64_t status(bool clear, int64_t device) {
   return static_cast<int64_t>(v);
 }
 
+int64_t launch_count() { return static_cast<int64_t>(wd_launch_count()); }
+
 void set_gate_up_path(int64_t path) { check_rc(wd_set_gate_up_path(static_cast<int>(path))); }
 void set_down_path(int64_t path) { check_rc(wd_set_down_path(static_cast<int>(path))); }
 void set_ffn_path(int64_t path) { check_rc(wd_set_ffn_path(static_cast<int>(path))); }
@@ -256,6 +258,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits"), py::arg("topk"), py::arg("renormalize") = true);
   m.def("status", &status, "Read (and clear) the device status word of the library",
         py::arg("clear") = true, py::arg("device") = 0);
+  m.def("launch_count", &launch_count,
+        "Kernels this library has enqueued in this process (graph captures count what they record)");
   m.def("set_gate_up_path", &set_gate_up_path,
         "gate_up kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
         py::arg("path"));

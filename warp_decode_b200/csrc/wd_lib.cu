@@ -46,6 +46,11 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+// Kernels enqueued by this library in this process (wd_launch_count).
+std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 constexpr int kMaxDevices = 64;
 
 struct DeviceInfo {
@@ -348,6 +353,7 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
           : cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>, tm_w, tm_x, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("gate_up (tensor core) launch: ") + cudaGetErrorString(err));
+  note_launch();
   return WD_OK;
 }
 
@@ -462,6 +468,7 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
                 : cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_kernel<FMT, wdb::ROUTE_LARGE>, a);
     if (err != cudaSuccess)
       return fail(WD_ERR_CUDA, std::string("gate_up launch: ") + cudaGetErrorString(err));
+    note_launch();
   }
   return WD_OK;
 }
@@ -602,6 +609,7 @@ int down_tc_launch(const DeviceInfo* dev, const void* h, const void* w, const in
                      : cudaLaunchKernelEx(&cfg, wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>, tm, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("down (tensor core) launch: ") + cudaGetErrorString(err));
+  note_launch();
   return WD_OK;
 }
 
@@ -720,6 +728,7 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
                 : cudaLaunchKernelEx(&cfg, wdb::moe_down_kernel<FMT, wdb::ROUTE_LARGE>, a);
     if (err != cudaSuccess)
       return fail(WD_ERR_CUDA, std::string("down launch: ") + cudaGetErrorString(err));
+    note_launch();
   }
   return WD_OK;
 }
@@ -848,6 +857,7 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
                        : cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel<false>, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("ffn launch: ") + cudaGetErrorString(err));
+  note_launch();
   return WD_OK;
 }
 
@@ -878,6 +888,8 @@ wdb::TpArgs make_tp_args(const TpComm* c) {
 extern "C" {
 
 int wd_version(void) { return 100; }
+
+unsigned long long wd_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* wd_error_string(int err) {
   switch (err) {
@@ -968,6 +980,7 @@ int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("router launch: ") + cudaGetErrorString(err));
+  note_launch();
   return WD_OK;
 }
 
