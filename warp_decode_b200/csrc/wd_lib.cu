@@ -94,6 +94,8 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_kernel<wdb::W_E4M3, wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_mx_kernel<wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_gate_up_tc_mx_kernel<wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<false, wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_down_tc_kernel<true, wdb::ROUTE_ANY>),
@@ -154,6 +156,13 @@ int check_common(int B, int E, int topk, int hidden, int inter) {
 #endif
 #ifndef WD_DTC_MIN_TOKENS
 #define WD_DTC_MIN_TOKENS 2
+#endif
+// MXFP8 weights: tensor cores (on-chip E4M3 decode) from this many tokens.
+// Measured gate_up (H 2048, I 768, E 128, top-8, cold, B200), tensor cores vs
+// SIMT: B = 2 34.9 vs 32.7 us, B = 4 47.2 vs 57.2, B = 8 74.8 vs 96.3,
+// B = 16 106.5 vs 174.8.
+#ifndef WD_TC_MX_MIN_TOKENS
+#define WD_TC_MX_MIN_TOKENS 4
 #endif
 #ifndef WD_TC_KCH
 #define WD_TC_KCH 4
@@ -226,19 +235,19 @@ EncodeTiledFn encode_tiled() {
 
 // How many clusters of `cl` gate_up CTAs with `smem` bytes each can be
 // resident at once (occupancy calculator; cached per device and shape).
-int gate_up_tc_active_clusters(int cl, int smem) {
+int gate_up_tc_active_clusters(int cl, int smem, bool mx = false) {
   static std::mutex mu;
-  static std::vector<std::array<int, 4>> cache;  // {device, cl, smem, clusters}
+  static std::vector<std::array<int, 5>> cache;  // {device, cl, smem, mx, clusters}
   int devno = 0;
   cudaGetDevice(&devno);
   {
     std::lock_guard<std::mutex> lock(mu);
     for (const auto& c : cache)
-      if (c[0] == devno && c[1] == cl && c[2] == smem) return c[3];
+      if (c[0] == devno && c[1] == cl && c[2] == smem && c[3] == (int)mx) return c[4];
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)cl);
-  cfg.blockDim = dim3(wdb::TC_THREADS);
+  cfg.blockDim = dim3(mx ? wdb::TC_MX_THREADS : wdb::TC_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -248,15 +257,15 @@ int gate_up_tc_active_clusters(int cl, int smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int nc = 0;
-  // All instantiations have the same launch shape and resources.
-  if (cudaOccupancyMaxActiveClusters(&nc, (const void*)wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>,
-                                     &cfg) !=
-      cudaSuccess) {
+  // All instantiations of one kernel have the same launch shape and resources.
+  const void* fn = mx ? (const void*)wdb::moe_gate_up_tc_mx_kernel<wdb::ROUTE_LARGE>
+                      : (const void*)wdb::moe_gate_up_tc_kernel<wdb::ROUTE_LARGE>;
+  if (cudaOccupancyMaxActiveClusters(&nc, fn, &cfg) != cudaSuccess) {
     cudaGetLastError();
     nc = 0;
   }
   std::lock_guard<std::mutex> lock(mu);
-  cache.push_back({devno, cl, smem, nc});
+  cache.push_back({devno, cl, smem, (int)mx, nc});
   return nc;
 }
 
@@ -330,6 +339,8 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
   a.npad = npad;
   a.kch = kch;
   a.cl = cl;
+  a.conv = 0;
+  a.xstages = 0;
   const long long work = (long long)n * n_tiles;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -357,6 +368,117 @@ int gate_up_tc_launch(const DeviceInfo* dev, const void* x, const void* w, const
   return WD_OK;
 }
 
+// Tensor-core gate_up with MXFP8 weights for one launch chunk of bn <= 16
+// tokens: E4M3 boxes of 128 K-bytes x 128 rows and their scale boxes are
+// decoded to bf16 on chip by the kernel's converter warps.
+int gate_up_tc_mx_launch(const DeviceInfo* dev, const void* x, const uint8_t* w,
+                         const uint8_t* wscale, const int32_t* ids, void* out, int bn, int E,
+                         int topk, int hidden, int inter, uint32_t* status, cudaStream_t s) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap tm_w, tm_x, tm_s;
+  const cuuint32_t ones[4] = {1, 1, 1, 1};
+  // E4M3 bytes [E, 2I, H] and scales [E, 2I, H / 32], both viewed as
+  // (k, neuron, gate|up, expert); 64 gate rows then the matching up rows.
+  const cuuint64_t wdim[4] = {(cuuint64_t)hidden, (cuuint64_t)inter, 2, (cuuint64_t)E};
+  const cuuint64_t wstr[3] = {(cuuint64_t)hidden, (cuuint64_t)inter * hidden,
+                              (cuuint64_t)2 * inter * hidden};
+  const cuuint32_t wbox[4] = {128, (cuuint32_t)wdb::TC_NEUR, 2, 1};
+  CUresult cr = enc(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(w), wdim, wstr,
+                    wbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    WD_TC_L2PROMO, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (MXFP8 w_gate_up) encode failed");
+  const cuuint64_t nb = (cuuint64_t)hidden / 32;
+  const cuuint64_t sdim[4] = {nb, (cuuint64_t)inter, 2, (cuuint64_t)E};
+  const cuuint64_t sstr[3] = {nb, (cuuint64_t)inter * nb, (cuuint64_t)2 * inter * nb};
+  const cuuint32_t sbox[4] = {16, (cuuint32_t)wdb::TC_NEUR, 2, 1};
+  cr = enc(&tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(wscale), sdim, sstr, sbox,
+           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (MXFP8 scales) encode failed");
+  const cuuint64_t xdim[2] = {(cuuint64_t)hidden, (cuuint64_t)bn};
+  const cuuint64_t xstr[1] = {(cuuint64_t)hidden * 2};
+  const int npad = (bn + 15) / 16 * 16;
+  const cuuint32_t xbox[2] = {(cuuint32_t)wdb::TC_BK, (cuuint32_t)npad};
+  cr = enc(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdim, xstr, xbox,
+           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (x) encode failed");
+
+  const int n = bn * topk;
+  const int budget = dev->smem_optin - 2048;
+  // Two converted boxes between converters and MMAs; E4M3 stages and x
+  // stages in equal numbers (the single producer thread issues both in stage
+  // order, so a shallower x ring would hold back the weight stream), as many
+  // as fit.
+  constexpr int kConv = 2;
+  auto plan = [&](int cl, int* stages_out) {
+    int st = 6;
+    while (st > 2 && wdb::gate_up_tc_mx_smem_bytes(st, st, kConv, npad, n, E, cl) > budget) --st;
+    *stages_out = st;
+    return wdb::gate_up_tc_mx_smem_bytes(st, st, kConv, npad, n, E, cl);
+  };
+  // Split K over clusters when items are few (the bf16 kernel's cost model).
+  const int n_tiles = (inter + wdb::TC_NEUR - 1) / wdb::TC_NEUR;
+  const double u_est =
+      E * (1.0 - std::pow(1.0 - std::min(topk, E) / (double)E, (double)bn));
+  const int items_est = std::max(1, (int)std::ceil(u_est)) * n_tiles;
+  int cl = 1, stages = 0, ncl = 0;
+  int smem = plan(1, &stages);
+  double best = 1e30;
+  const int nks_all = hidden / wdb::TC_MX_STAGE_K;
+  for (int c = 1; c <= std::min(WD_TC_MAX_CLUSTER, nks_all); ++c) {  // >= 1 stage per CTA
+    int st = 0;
+    const int sm = plan(c, &st);
+    if (sm > budget) continue;
+    int nc = dev->sm_count / c;
+    if (c > 1) nc = std::min(nc, gate_up_tc_active_clusters(c, sm, true));
+    if (nc < 1) continue;
+    const double cost = std::ceil((double)items_est / nc) / c + 0.02 * (c - 1);
+    if (cost < best) { best = cost; cl = c; stages = st; smem = sm; ncl = nc; }
+  }
+  if (smem > budget) return fail(WD_ERR_UNSUPPORTED, "shared memory budget exceeded");
+  wdb::GateUpTcArgs a;
+  a.ids = ids;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.status = status;
+  a.B = bn; a.E = E; a.K = topk; a.H = hidden; a.I = inter;
+  a.stages = stages;
+  a.npad = npad;
+  a.kch = 0;
+  a.cl = cl;
+  a.conv = kConv;
+  a.xstages = stages;
+  const long long work = (long long)n * n_tiles;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  if (cl > 1) {
+    cfg.gridDim = dim3((unsigned)(ncl * cl));
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  } else {
+    cfg.gridDim = dim3((unsigned)std::min<long long>(dev->sm_count, work));
+  }
+  cfg.blockDim = dim3(wdb::TC_MX_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = s;
+  cudaError_t err =
+      n <= 64
+          ? cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_mx_kernel<wdb::ROUTE_SMALL>, tm_w, tm_x,
+                               tm_s, a)
+          : cudaLaunchKernelEx(&cfg, wdb::moe_gate_up_tc_mx_kernel<wdb::ROUTE_LARGE>, tm_w, tm_x,
+                               tm_s, a);
+  if (err != cudaSuccess)
+    return fail(WD_ERR_CUDA,
+                std::string("gate_up (MXFP8, tensor core) launch: ") + cudaGetErrorString(err));
+  note_launch();
+  return WD_OK;
+}
+
 // Whether a call of B tokens runs on the tensor-core kernel (in launches of
 // at most TC_NMAX tokens).
 bool gate_up_tc_applies(int B, int E, int hidden) {
@@ -364,6 +486,16 @@ bool gate_up_tc_applies(int B, int E, int hidden) {
   if (p == 1) return false;
   if (E > wdb::MAX_DEDUP_E || hidden % 8 != 0) return false;
   return p == 2 || B >= WD_TC_MIN_TOKENS;
+}
+
+// The same for MXFP8 weights (in launches of at most TC_MX_NMAX tokens).
+// The scale rows (hidden / 32 bytes) must be tensor-map strides (16-byte
+// multiples), so hidden % 512 == 0.
+bool gate_up_tc_mx_applies(int B, int E, int hidden) {
+  const int p = gate_up_path();
+  if (p == 1) return false;
+  if (E > wdb::MAX_DEDUP_E || hidden % 512 != 0) return false;
+  return p == 2 || B >= WD_TC_MX_MIN_TOKENS;
 }
 
 template <int FMT>
@@ -387,9 +519,10 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   if ((rc = device_info(&dev))) return rc;
 
   constexpr int WB = FMT == wdb::W_BF16 ? 2 : 1;
-  const bool tc = FMT == wdb::W_BF16 && gate_up_tc_applies(B, E, hidden);
+  const bool tc = FMT == wdb::W_BF16 ? gate_up_tc_applies(B, E, hidden)
+                                     : gate_up_tc_mx_applies(B, E, hidden);
   int tb = std::max(1, wdb::MAX_SLOTS / topk);  // tokens per launch
-  if (tc) tb = std::min(tb, wdb::TC_NMAX);
+  if (tc) tb = std::min(tb, FMT == wdb::W_BF16 ? wdb::TC_NMAX : wdb::TC_MX_NMAX);
   if ((long long)std::min(tb, B) * topk * inter >= (1LL << 31))
     return fail(WD_ERR_UNSUPPORTED, "B*topk*inter per launch must be < 2^31");
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -397,10 +530,13 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
     const int bn = std::min(tb, B - b0);
     const int n = bn * topk;
     if (tc) {
-      rc = gate_up_tc_launch(dev, reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden,
-                             w, ids + (size_t)b0 * topk,
-                             reinterpret_cast<__nv_bfloat16*>(out) + (size_t)b0 * topk * inter, bn,
-                             E, topk, hidden, inter, status, s);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)b0 * hidden;
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)b0 * topk * inter;
+      rc = FMT == wdb::W_BF16
+               ? gate_up_tc_launch(dev, xb, w, ids + (size_t)b0 * topk, ob, bn, E, topk, hidden,
+                                   inter, status, s)
+               : gate_up_tc_mx_launch(dev, xb, w, wscale, ids + (size_t)b0 * topk, ob, bn, E,
+                                      topk, hidden, inter, status, s);
       if (rc) return rc;
       continue;
     }
