@@ -25,9 +25,17 @@
 //    2..5 = gather (one h slice each in flight), 6..9 = epilogue (TMEM lane
 //    quarter warp % 4).  Weight stages, h slices and D buffers are rings
 //    with full/empty mbarriers; every wait is bounded.
+//  * MXFP8 weights (moe_down_tc_mx_kernel): the weight stages hold E4M3
+//    boxes of 128 K-bytes x 128 rows (no swizzle) and each item's UE8M0
+//    scales (128 rows x inter / 32 bytes, one bulk copy) sit in a ring of
+//    two; eight more warps (10..17) decode each box into two bf16 K-chunks
+//    of the 128-byte-swizzled layout in a ring of converted tiles (the
+//    decode of the MXFP8 gate_up kernel) and free the E4M3 stage as soon as
+//    it is decoded; the MMA reads A from the converted tiles.
 #pragma once
 
 #include "wd_down.cuh"
+#include "wd_gate_up_tc.cuh"
 #include "wd_tc.cuh"
 
 namespace wdb {
@@ -43,6 +51,10 @@ constexpr int DTC_THREADS = (2 + DTC_GW + 4) * 32;
 constexpr int DTC_A_CHUNK = DTC_M * DTC_BK * 2;  // 16 KB of weights
 constexpr int DTC_B_CHUNK = DTC_N * DTC_BK * 2;  // 2 KB of h rows
 constexpr uint32_t DTC_TMEM_COLS = DTC_ND * DTC_N < 32 ? 32 : DTC_ND * DTC_N;
+constexpr int DTC_MX_CW = 8;                     // MXFP8 converter warps
+constexpr int DTC_MX_THREADS = DTC_THREADS + DTC_MX_CW * 32;
+constexpr int DTC_MX_BOX = DTC_M * 128;          // E4M3 box: 128 rows x 128 K (bytes)
+constexpr int DTC_MX_NMAX = 16;                  // tokens per MXFP8 launch
 
 // Fused one-shot all-reduce over the ranks of a tensor-parallel group (one
 // process per GPU, peer memory opened through CUDA IPC).  Every rank's
@@ -89,6 +101,8 @@ struct DownTcArgs {
                            // ring turn ahead, so mbarrier parities cannot alias)
   int cl;                  // CTAs per cluster (1, 2, 4 or 8)
   TpArgs tp;               // fused all-reduce (tp.world > 1): out = bf16 sum over ranks
+  const uint8_t* wscale;   // MXFP8: UE8M0 scales [E, H, I / 32] (nullptr for bf16)
+  int conv;                // MXFP8: converted-box ring depth
 };
 
 __host__ __device__ inline int down_tc_kc(int I) { return (I + DTC_BK - 1) / DTC_BK; }
@@ -101,12 +115,21 @@ __host__ inline int down_tc_smem_bytes(int stages, int sc, int nbuf, int I, int 
          CTRL_INTS * 4 + route_smem_bytes(n, E, true);
 }
 
-// kTP: the fused all-reduce variant (tp.world > 1); the plain kernel carries
-// none of its code.  kRoute: routing code compiled for this launch's slot
-// count (RouteMode).
-template <bool kTP, int kRoute>
-__global__ void __launch_bounds__(DTC_THREADS, 1)
-    moe_down_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const DownTcArgs a) {
+// MXFP8: weight stages of sc / 2 E4M3 boxes, two scale slots of 4 * I bytes,
+// `conv` converted boxes; the rest as for bf16.
+__host__ inline int down_tc_mx_smem_bytes(int stages, int sc, int nbuf, int conv, int I, int B,
+                                          int n, int E) {
+  return 1024 + stages * (sc / 2) * DTC_MX_BOX + nbuf * sc * DTC_B_CHUNK + conv * TC_MX_CONV +
+         2 * 4 * I + B * DTC_M * 4 + ((n * 4 + 127) / 128) * 128 +
+         (2 * stages + 2 * nbuf + 2 * DTC_ND + 1 + 2 * conv + 4) * 8 + 16 + CTRL_INTS * 4 +
+         route_smem_bytes(n, E, true);
+}
+
+// Body of both kernels.  kTP: the fused all-reduce variant (tp.world > 1);
+// the plain kernel carries none of its code.  kMx: MXFP8 weights.  kRoute:
+// routing code compiled for this launch's slot count (RouteMode).
+template <bool kTP, bool kMx, int kRoute>
+__device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const DownTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* base = smem_raw + pad;
@@ -116,11 +139,15 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   const int n = a.B * a.K;
   const int SC = a.sc;              // K chunks per weight stage
   const int nst = (kc + SC - 1) / SC;  // weight stages per item
-  const int SB = SC * DTC_A_CHUNK;  // bytes of one weight stage
+  const int SB = kMx ? (SC / 2) * DTC_MX_BOX : SC * DTC_A_CHUNK;  // bytes of one weight stage
   const int BB = SC * DTC_B_CHUNK;  // bytes of one h slice (one weight stage's K range)
+  const int CS = kMx ? a.conv : 0;
+  const int SCB = kMx ? 4 * I : 0;  // MXFP8: bytes of one item's scales (128 rows x I / 32)
   uint8_t* wring = base;
   uint8_t* bring = wring + (size_t)S * SB;
-  float* Y = reinterpret_cast<float*>(bring + (size_t)NB * BB);  // [B][128]
+  uint8_t* conv = bring + (size_t)NB * BB;  // MXFP8: [CS] converted boxes
+  uint8_t* sring = conv + (size_t)CS * TC_MX_CONV;  // MXFP8: [2] item scales
+  float* Y = reinterpret_cast<float*>(sring + 2 * SCB);  // [B][128]
   float* s_scale = Y + a.B * DTC_M;
   uint64_t* wfull = reinterpret_cast<uint64_t*>(s_scale + ((n * 4 + 127) / 128) * 32);
   uint64_t* wempty = wfull + S;
@@ -129,7 +156,11 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   uint64_t* dfull = bempty + NB;
   uint64_t* dempty = dfull + DTC_ND;
   uint64_t* done = dempty + DTC_ND;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* cfull = done + 1;      // MXFP8: [CS] converted box written
+  uint64_t* cempty = cfull + CS;   // MXFP8: [CS] converted box read by the MMAs
+  uint64_t* sfull = cempty + CS;   // MXFP8: [2] item scales landed
+  uint64_t* sempty = sfull + (kMx ? 2 : 0);  // MXFP8: [2] item scales decoded
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + (kMx ? 2 : 0));
   volatile int* ctrl = reinterpret_cast<volatile int*>(tmem_slot + 4);
   int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
   const RouteSmem r = route_carve(route_base, n, a.E, true);
@@ -142,7 +173,17 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&wfull[s], 1);
-      mbar_init(&wempty[s], 1);
+      mbar_init(&wempty[s], kMx ? DTC_MX_CW : 1);  // MXFP8: freed by the converters
+    }
+    if constexpr (kMx) {
+      for (int c = 0; c < CS; ++c) {
+        mbar_init(&cfull[c], DTC_MX_CW);
+        mbar_init(&cempty[c], 1);
+      }
+      for (int c = 0; c < 2; ++c) {
+        mbar_init(&sfull[c], 1);
+        mbar_init(&sempty[c], DTC_MX_CW);
+      }
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(&bfull[b], 1);
@@ -200,8 +241,9 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     // ---------------- weight producer ----------------
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
+    uint32_t ni = 0, nsi = 0;  // MXFP8: items started, scale copies issued
     bool ok = true;
-    if (nst == 1) {
+    if (!kMx && nst == 1) {
       // one stage per item (inter <= 256)
       for (int g = g_first; g < nsg; g = next_item(g)) {
         const int slot = (int)(it % (uint32_t)S);
@@ -221,13 +263,37 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         ++it;
       }
     } else
-    for (int g = g_first; ok && g < nsg; g = next_item(g)) {
+    for (int g = g_first; ok && g < nsg; g = next_item(g), ++ni) {
+      if constexpr (kMx) {
+        // The item's scales: rows [j0, j0 + 128) x I / 32 bytes, contiguous.
+        if (lane == 0) {
+          const int sb = (int)(ni & 1u);
+          if (!wait(&sempty[sb], ((ni >> 1) & 1u) ^ 1u)) {
+            ok = false;
+          } else {
+            mbar_arrive_expect_tx(&sfull[sb], (uint32_t)SCB);
+            bulk_g2s(sring + (size_t)sb * SCB,
+                     a.wscale + ((size_t)r.sg_exp[g] * a.H + j0) * (size_t)(I / 32), (uint32_t)SCB,
+                     &sfull[sb], pol);
+            nsi = ni + 1;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
       for (int sj = 0; sj < nst; ++sj) {
         const int slot = (int)(it % (uint32_t)S);
         const int c0 = sj * SC, nc = min(SC, kc - c0);
         if (lane == 0) {
           if (!wait(&wempty[slot], ((it / (uint32_t)S) & 1u) ^ 1u)) {
             ok = false;
+          } else if constexpr (kMx) {
+            // nc / 2 E4M3 boxes of 128 K-bytes (inter % 128 == 0 on this path)
+            uint8_t* st = wring + (size_t)slot * SB;
+            mbar_arrive_expect_tx(&wfull[slot], (uint32_t)((nc / 2) * DTC_MX_BOX));
+            for (int b = 0; b < nc / 2; ++b)
+              tma_load_3d(st + b * DTC_MX_BOX, &tm_w, (c0 + 2 * b) * DTC_BK, j0, r.sg_exp[g],
+                          &wfull[slot], pol);
           } else {
             uint8_t* st = wring + (size_t)slot * SB;
             mbar_arrive_expect_tx(&wfull[slot], (uint32_t)(nc * DTC_A_CHUNK));
@@ -249,14 +315,23 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
                globaltimer_ns() - t0 < WD_WAIT_LIMIT_NS) {
         }
       }
+      if constexpr (kMx) {
+        const uint32_t slo = nsi > 2u ? nsi - 2u : 0u;
+        for (uint32_t i = slo; i < nsi; ++i) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&sfull[i & 1u], (i >> 1) & 1u) &&
+                 globaltimer_ns() - t0 < WD_WAIT_LIMIT_NS) {
+          }
+        }
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t it = 0, its = 0;  // items, weight stages
+      uint32_t it = 0, its = 0, ci = 0;  // items, weight stages, converted boxes
       bool issued = false, ok = true;
       const uint32_t idesc = tc_idesc_bf16(DTC_M, DTC_N);
-      if (nst == 1) {
+      if (!kMx && nst == 1) {
         // one stage per item (inter <= 256)
         for (int g = g_first; g < nsg; g = next_item(g)) {
           const int slot = (int)(it % (uint32_t)S);
@@ -291,25 +366,56 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         for (int sj = 0; sj < nst; ++sj, ++its) {
           const int slot = (int)(its % (uint32_t)S);
           const int hb = (int)(its % (uint32_t)NB);
-          if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u) ||
-              !wait(&bfull[hb], (its / (uint32_t)NB) & 1u)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint8_t* W = wring + (size_t)slot * SB;
-          const uint8_t* Bt = bring + (size_t)hb * BB;
           const int c0 = sj * SC, nc = min(SC, kc - c0);
-          for (int cc = 0; cc < nc; ++cc) {
-            const uint64_t ad = tc_desc_sw128(smem_u32(W + cc * DTC_A_CHUNK));
-            const uint64_t bd = tc_desc_sw128(smem_u32(Bt + cc * DTC_B_CHUNK));
+          if constexpr (kMx) {
+            // A from the converted boxes of this stage (two K-chunks each),
+            // B from the stage's h slice; the converters free the E4M3 stage.
+            if (!wait(&bfull[hb], (its / (uint32_t)NB) & 1u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint8_t* Bt = bring + (size_t)hb * BB;
+            for (int b = 0; b < nc / 2; ++b, ++ci) {
+              const int cs = (int)(ci % (uint32_t)CS);
+              if (!wait(&cfull[cs], (ci / (uint32_t)CS) & 1u)) { ok = false; break; }
+              tc_fence_after();
+              for (int hh = 0; hh < 2; ++hh) {
+                const int cc = 2 * b + hh;
+                const uint64_t ad =
+                    tc_desc_sw128(smem_u32(conv + (size_t)cs * TC_MX_CONV + hh * DTC_A_CHUNK));
+                const uint64_t bd = tc_desc_sw128(smem_u32(Bt + cc * DTC_B_CHUNK));
 #pragma unroll
-            for (int kk = 0; kk < DTC_BK / 16; ++kk)
-              tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc, ((c0 + cc) | kk) != 0 ? 1u : 0u);
+                for (int kk = 0; kk < DTC_BK / 16; ++kk)
+                  tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc,
+                              ((c0 + cc) | kk) != 0 ? 1u : 0u);
+              }
+              tc_commit(&cempty[cs]);
+              issued = true;
+            }
+            if (!ok) break;
+            tc_commit(&bempty[hb]);
+          } else {
+            if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u) ||
+                !wait(&bfull[hb], (its / (uint32_t)NB) & 1u)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint8_t* W = wring + (size_t)slot * SB;
+            const uint8_t* Bt = bring + (size_t)hb * BB;
+            for (int cc = 0; cc < nc; ++cc) {
+              const uint64_t ad = tc_desc_sw128(smem_u32(W + cc * DTC_A_CHUNK));
+              const uint64_t bd = tc_desc_sw128(smem_u32(Bt + cc * DTC_B_CHUNK));
+#pragma unroll
+              for (int kk = 0; kk < DTC_BK / 16; ++kk)
+                tc_mma_bf16(dt, ad + 2u * kk, bd + 2u * kk, idesc,
+                            ((c0 + cc) | kk) != 0 ? 1u : 0u);
+            }
+            tc_commit(&wempty[slot]);
+            tc_commit(&bempty[hb]);
+            issued = true;
           }
-          tc_commit(&wempty[slot]);
-          tc_commit(&bempty[hb]);
-          issued = true;
         }
         if (!ok) break;
         tc_commit(&dfull[d]);
@@ -330,7 +436,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     const int vecs = I / 8;  // 16-byte pieces per h row
     uint32_t its = 0;
     bool got = true;
-    if (nst == 1) {
+    if (!kMx && nst == 1) {
       // one slice per item (inter <= 256): the item loop alone
       for (int g = g_first; g < nsg; g = next_item(g), ++its) {
         if ((int)(its % DTC_GW) != gw) continue;
@@ -376,7 +482,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         if (lane == 0) mbar_arrive(&bfull[hb]);
       }
     }
-  } else {
+  } else if (warp < 2 + DTC_GW + 4) {
     // ---------------- epilogue: row j = 32 * (warp % 4) + lane ------------
     const int q = warp & 3;
     const int j = 32 * q + lane;
@@ -402,6 +508,68 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[d]);
+    }
+  } else {
+    // ---------------- MXFP8 converters: warps 10..17 ----------------
+    // The mapping of the MXFP8 gate_up converters: per box, warp cw and unit
+    // u cover rows 32u + 4cw .. +3 and all eight 16-byte K units of each
+    // row, every quarter warp on 8 different 16-byte bank groups.  Scale
+    // byte of (row, K block kb): sring[row * (I / 32) + kb].
+    if constexpr (kMx) {
+    const int cw = warp - (2 + DTC_GW + 4);
+    const int c16 = lane & 7;
+    const int rsub = 2 * ((lane >> 4) & 1) + (((lane >> 2) & 1) ^ ((lane >> 3) & 1));
+    const int nb = I / 32;
+    uint32_t its = 0, ci = 0, ni = 0;
+    bool ok = true;
+    for (int g = g_first; ok && g < nsg; g = next_item(g), ++ni) {
+      const int sb = (int)(ni & 1u);
+      if (!wait(&sfull[sb], (ni >> 1) & 1u)) break;
+      const uint8_t* sc = sring + (size_t)sb * SCB;
+      for (int sj = 0; sj < nst; ++sj, ++its) {
+        const int slot = (int)(its % (uint32_t)S);
+        if (!wait(&wfull[slot], (its / (uint32_t)S) & 1u)) { ok = false; break; }
+        const int c0 = sj * SC, nc = min(SC, kc - c0);
+        const uint8_t* w8 = wring + (size_t)slot * SB;
+        for (int b = 0; b < nc / 2; ++b, ++ci) {
+          const int cs = (int)(ci % (uint32_t)CS);
+          if (!wait(&cempty[cs], ((ci / (uint32_t)CS) & 1u) ^ 1u)) { ok = false; break; }
+          uint8_t* dst = conv + (size_t)cs * TC_MX_CONV;
+          const uint8_t* src = w8 + b * DTC_MX_BOX;
+          const int kb0 = 2 * (c0 + 2 * b);  // first 32-element block of the box
+          constexpr int NU = DTC_M / (4 * DTC_MX_CW);
+          uint4 v[NU];
+          uint32_t sbyte[NU];
+#pragma unroll
+          for (int u = 0; u < NU; ++u) {
+            const int row = 4 * DTC_MX_CW * u + 4 * cw + rsub;
+            v[u] = lds16(src + row * 128 + c16 * 16);
+            sbyte[u] = sc[row * nb + kb0 + (c16 >> 1)];
+          }
+#pragma unroll
+          for (int u = 0; u < NU; ++u) {
+            const int row = 4 * DTC_MX_CW * u + 4 * cw + rsub;
+            uint32_t p[8];
+            mx_decode_scaled(v[u], sbyte[u], p);
+            uint8_t* drow = dst + (c16 >> 2) * DTC_A_CHUNK + row * 128;
+            const int u0 = (c16 & 3) * 2;
+            *reinterpret_cast<uint4*>(drow + ((u0 ^ (row & 7)) << 4)) =
+                make_uint4(p[0], p[1], p[2], p[3]);
+            *reinterpret_cast<uint4*>(drow + (((u0 + 1) ^ (row & 7)) << 4)) =
+                make_uint4(p[4], p[5], p[6], p[7]);
+          }
+          fence_proxy_async_smem();  // generic writes -> tensor-core reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&cfull[cs]);
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty[slot]);  // E4M3 stage decoded
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[sb]);  // item scales no longer read
+    }
     }
   }
 
@@ -502,6 +670,20 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   if (tp && threadIdx.x == 0)
     for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += (int)gridDim.x) a.tp.epochs[c2] = ep;
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile
+}
+
+template <bool kTP, int kRoute>
+__global__ void __launch_bounds__(DTC_THREADS, 1)
+    moe_down_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const DownTcArgs a) {
+  down_tc_body<kTP, false, kRoute>(tm_w, a);
+}
+
+// MXFP8 weights: tm_w over the E4M3 bytes [E, H, I], a.wscale the UE8M0
+// scales [E, H, I / 32].  Single GPU (no fused all-reduce).
+template <int kRoute>
+__global__ void __launch_bounds__(DTC_MX_THREADS, 1)
+    moe_down_tc_mx_kernel(const __grid_constant__ CUtensorMap tm_w, const DownTcArgs a) {
+  down_tc_body<false, true, kRoute>(tm_w, a);
 }
 
 }  // namespace wdb
