@@ -99,7 +99,7 @@ struct DownTcArgs {
   int nbuf;                // h slices (the K range of one weight stage of one
                            // item), >= DTC_GW (a gather warp is at most one
                            // ring turn ahead, so mbarrier parities cannot alias)
-  int cl;                  // CTAs per cluster (1, 2, 4 or 8)
+  int cl;                  // CTAs per cluster (1 to 8)
   TpArgs tp;               // fused all-reduce (tp.world > 1): out = bf16 sum over ranks
   const uint8_t* wscale;   // MXFP8: UE8M0 scales [E, H, I / 32] (nullptr for bf16)
   int conv;                // MXFP8: converted-box ring depth
@@ -576,16 +576,18 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   tc_fence_before();
   __syncthreads();
   // Y is final: release it to the cluster, free TMEM meanwhile, then sum the
-  // CL partial tiles in rank order; CTA `rank` writes rows
-  // [rank * 128 / CL, (rank + 1) * 128 / CL) of the tile, 4 rows per thread.
+  // CL partial tiles in rank order; CTA `rank` writes rows [lo, hi) of the
+  // tile (the 32 four-row units split as evenly as CL allows; CL need not
+  // divide 128), 4 rows per thread.
   if (CL > 1) cluster_arrive();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, DTC_TMEM_COLS);
   }
   if (CL > 1) cluster_wait();
-  const int rpr = DTC_M / CL;   // multiple of 16
-  const int q4 = rpr / 4;
+  const int lo = (rank * (DTC_M / 4) / CL) * 4;
+  const int hi = ((rank + 1) * (DTC_M / 4) / CL) * 4;
+  const int q4 = (hi - lo) / 4;
   const bool tp = kTP && a.tp.world > 1;
   const uint32_t ep = tp_ep;  // this call's epoch (read at kernel start)
   const int slot = (int)(ep & 1u);
@@ -594,7 +596,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   };
   bool tp_ok = true;
   for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
-    const int t = i / q4, jj = rank * rpr + 4 * (i - t * q4);
+    const int t = i / q4, jj = lo + 4 * (i - t * q4);
     const float* src = &Y[t * DTC_M + jj];
     float4 acc;
     if (CL > 1) {

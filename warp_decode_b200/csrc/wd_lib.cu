@@ -611,9 +611,11 @@ int gate_up_impl(const void* x, const uint8_t* w, const uint8_t* wscale, const i
   return WD_OK;
 }
 
-// Largest cluster size CL in {8, 4, 2, 1} such that the ceil(hidden / 128)
-// row tiles times CL CTAs fit on the SMs at once (checked with the
-// occupancy calculator for this launch configuration); 0 if none.
+// Largest cluster size CL <= 8 such that the ceil(hidden / 128) row tiles
+// times CL CTAs fit on the SMs at once (checked with the occupancy
+// calculator for this launch configuration); 0 if none.  Sizes that are not
+// powers of two matter for few tiles: at hidden 2048 (16 tiles) clusters of 8
+// of the MXFP8 kernel do not all fit, and 7 gives 112 CTAs where 4 gave 64.
 int down_tc_cluster(const DeviceInfo* dev, int hidden, int smem, bool mx = false) {
   static std::mutex mu;
   static std::vector<std::array<int, 5>> cache;  // {device, hidden, smem, mx, CL}
@@ -626,7 +628,7 @@ int down_tc_cluster(const DeviceInfo* dev, int hidden, int smem, bool mx = false
   }
   const int T = (hidden + wdb::DTC_M - 1) / wdb::DTC_M;
   int best = 0;
-  for (int cl : {8, 4, 2, 1}) {
+  for (int cl = 8; cl >= 1; --cl) {
     if (T * cl > dev->sm_count) continue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(T * cl));
@@ -666,11 +668,12 @@ bool down_tc_applies(int B, int E, int hidden, int inter, int sms) {
 // DTC_MX_NMAX tokens): whole 128-K E4M3 boxes (inter % 128 == 0), whole row
 // tiles and item scales that are 16-byte-aligned bulk copies (hidden % 128
 // == 0, hidden * inter % 512 == 0).
-// Automatic from 16 tokens.  Measured (H 2048, I 768, E 128, top-8, cold,
-// B200), tensor cores vs SIMT: B = 2 35.0 vs 32.7 us, B = 4 57.4 vs 38.9,
-// B = 8 86.2 vs 78.5, B = 16 133.2 vs 189.9.
+// Automatic from 8 tokens.  Measured (H 2048, I 768, E 128, top-8, cold,
+// B200; clusters of 7 over the 16 row tiles), tensor cores vs SIMT: B = 2
+// 30.4 vs 32.1 us, B = 4 40.9 vs 38.9, B = 8 65.2 vs 78.0, B = 16 94.2 vs
+// 189.9.
 #ifndef WD_DTC_MX_MIN_TOKENS
-#define WD_DTC_MX_MIN_TOKENS 16
+#define WD_DTC_MX_MIN_TOKENS 8
 #endif
 bool down_tc_mx_applies(int B, int E, int hidden, int inter, int sms) {
   const int p = down_path();
