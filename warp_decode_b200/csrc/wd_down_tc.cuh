@@ -510,15 +510,11 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
       if (lane == 0) mbar_arrive(&dempty[d]);
     }
   } else {
-    // ---------------- MXFP8 converters: warps 10..17 ----------------
-    // The mapping of the MXFP8 gate_up converters: per box, warp cw and unit
-    // u cover rows 32u + 4cw .. +3 and all eight 16-byte K units of each
-    // row, every quarter warp on 8 different 16-byte bank groups.  Scale
-    // byte of (row, K block kb): sring[row * (I / 32) + kb].
+    // ---------------- MXFP8 converters: warps 10..17 (mx_convert_box) ----
+    // Scale byte of (row, K block kb): sring[row * (I / 32) + kb].
     if constexpr (kMx) {
+    static_assert(DTC_MX_CW == TC_MX_CW && DTC_M == TC_M, "shared box converter");
     const int cw = warp - (2 + DTC_GW + 4);
-    const int c16 = lane & 7;
-    const int rsub = 2 * ((lane >> 4) & 1) + (((lane >> 2) & 1) ^ ((lane >> 3) & 1));
     const int nb = I / 32;
     uint32_t its = 0, ci = 0, ni = 0;
     bool ok = true;
@@ -534,30 +530,9 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
         for (int b = 0; b < nc / 2; ++b, ++ci) {
           const int cs = (int)(ci % (uint32_t)CS);
           if (!wait(&cempty[cs], ((ci / (uint32_t)CS) & 1u) ^ 1u)) { ok = false; break; }
-          uint8_t* dst = conv + (size_t)cs * TC_MX_CONV;
-          const uint8_t* src = w8 + b * DTC_MX_BOX;
           const int kb0 = 2 * (c0 + 2 * b);  // first 32-element block of the box
-          constexpr int NU = DTC_M / (4 * DTC_MX_CW);
-          uint4 v[NU];
-          uint32_t sbyte[NU];
-#pragma unroll
-          for (int u = 0; u < NU; ++u) {
-            const int row = 4 * DTC_MX_CW * u + 4 * cw + rsub;
-            v[u] = lds16(src + row * 128 + c16 * 16);
-            sbyte[u] = sc[row * nb + kb0 + (c16 >> 1)];
-          }
-#pragma unroll
-          for (int u = 0; u < NU; ++u) {
-            const int row = 4 * DTC_MX_CW * u + 4 * cw + rsub;
-            uint32_t p[8];
-            mx_decode_scaled(v[u], sbyte[u], p);
-            uint8_t* drow = dst + (c16 >> 2) * DTC_A_CHUNK + row * 128;
-            const int u0 = (c16 & 3) * 2;
-            *reinterpret_cast<uint4*>(drow + ((u0 ^ (row & 7)) << 4)) =
-                make_uint4(p[0], p[1], p[2], p[3]);
-            *reinterpret_cast<uint4*>(drow + (((u0 + 1) ^ (row & 7)) << 4)) =
-                make_uint4(p[4], p[5], p[6], p[7]);
-          }
+          mx_convert_box(w8 + b * DTC_MX_BOX, conv + (size_t)cs * TC_MX_CONV, sc + kb0, nb, cw,
+                         lane);
           fence_proxy_async_smem();  // generic writes -> tensor-core reads
           __syncwarp();
           if (lane == 0) mbar_arrive(&cfull[cs]);

@@ -137,6 +137,47 @@ __device__ __forceinline__ void mx_decode_scaled(const uint4& v, uint32_t s, uin
   }
 }
 
+// One E4M3 box (128 rows x 128 K-bytes, rows 128 B apart, at src) -> two
+// bf16 K-chunks of the 128-byte-swizzled K-major layout at dst and dst +
+// 16 KB, run by all TC_MX_CW converter warps (cw = converter warp index).
+// The scale byte of (row, 16-byte unit c16) is sc[row * sc_row + (c16 >> 1)]
+// (sc already offset to the box's first 32-element block).
+//
+// Per box, warp cw and unit u < 4 cover rows 32u + 4cw .. +3, all eight
+// 16-byte K units (c16) of each row.  16-byte shared accesses are served per
+// quarter warp (8 lanes), so each quarter must touch 8 different 16-byte bank
+// groups: quarter q = 2 pair + half takes units 0-3 of row 2 pair + half and
+// units 4-7 of row 2 pair + (half ^ 1).  The loads then hit groups c16, and
+// the bf16 stores (swizzled unit (2 (c16 & 3) + t) ^ (row & 7), t = 0, 1)
+// hit two disjoint sets of four because the two rows differ in bit 0.  The
+// four units are independent (loads first, then decode and stores), so the
+// decode's integer chains overlap.
+__device__ __forceinline__ void mx_convert_box(const uint8_t* src, uint8_t* dst,
+                                               const uint8_t* sc, int sc_row, int cw, int lane) {
+  constexpr int NU = TC_M / (4 * TC_MX_CW);  // units per thread per box
+  const int c16 = lane & 7;
+  const int rsub = 2 * ((lane >> 4) & 1) + (((lane >> 2) & 1) ^ ((lane >> 3) & 1));
+  uint4 v[NU];
+  uint32_t sbyte[NU];
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const int row = 4 * TC_MX_CW * u + 4 * cw + rsub;
+    v[u] = lds16(src + row * 128 + c16 * 16);
+    sbyte[u] = sc[row * sc_row + (c16 >> 1)];
+  }
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const int row = 4 * TC_MX_CW * u + 4 * cw + rsub;
+    uint32_t p[8];
+    mx_decode_scaled(v[u], sbyte[u], p);
+    uint8_t* drow = dst + (c16 >> 2) * TC_A_BYTES + row * 128;
+    const int u0 = (c16 & 3) * 2;
+    *reinterpret_cast<uint4*>(drow + ((u0 ^ (row & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+    *reinterpret_cast<uint4*>(drow + (((u0 + 1) ^ (row & 7)) << 4)) =
+        make_uint4(p[4], p[5], p[6], p[7]);
+  }
+}
+
 // Body of both kernels.  kMx: MXFP8 weights (tm_w over E4M3 bytes, tm_s over
 // the scales, converter warps); else bf16 weights.  kRoute: routing code
 // compiled for this launch's slot count (RouteMode).
@@ -405,20 +446,9 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
     }
     __syncwarp();
   } else if (warp >= 6) {
-    // ---------------- MXFP8 converters: warps 6..13 ----------------
-    // Per box, warp w and unit u < 4 cover rows 32u + 4w .. +3, all eight
-    // 16-byte K units (c16) of each row.  16-byte shared accesses are served
-    // per quarter warp (8 lanes), so each quarter must touch 8 different
-    // 16-byte bank groups: quarter q = 2 pair + half takes units 0-3 of row
-    // 2 pair + half and units 4-7 of row 2 pair + (half ^ 1).  The loads then
-    // hit groups c16, and the bf16 stores (swizzled unit (2 (c16 & 3) + t) ^
-    // (row & 7), t = 0, 1) hit two disjoint sets of four because the two rows
-    // differ in bit 0.  The four units are independent (loads first, then
-    // decode and stores), so the decode's integer chains overlap.
+    // ---------------- MXFP8 converters: warps 6..13 (mx_convert_box) -----
     if constexpr (kMx) {
     const int cw = warp - 6;
-    const int c16 = lane & 7;
-    const int rsub = 2 * ((lane >> 4) & 1) + (((lane >> 2) & 1) ^ ((lane >> 3) & 1));
     uint32_t it = 0, ci = 0;
     bool ok = true;
     for (int t = cid; ok && t < items; t += G) {
@@ -433,29 +463,9 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
         for (int j = 0; j < 2; ++j, ++ci) {
           const int cs = (int)(ci % (uint32_t)CS);
           if (!wait(&cempty[cs], ((ci / (uint32_t)CS) & 1u) ^ 1u)) { ok = false; break; }
-          uint8_t* dst = conv + (size_t)cs * TC_MX_CONV;
-          const uint8_t* src = w8 + j * TC_MX_BOX;
-          constexpr int NU = TC_M / (4 * TC_MX_CW);  // units per thread per box
-          uint4 v[NU];
-          uint32_t sbyte[NU];
-#pragma unroll
-          for (int u = 0; u < NU; ++u) {
-            const int row = 4 * TC_MX_CW * u + 4 * cw + rsub;
-            v[u] = lds16(src + row * 128 + c16 * 16);
-            sbyte[u] = sc[row * 16 + sb0 + j * 4 + (c16 >> 1)];
-          }
-#pragma unroll
-          for (int u = 0; u < NU; ++u) {
-            const int row = 4 * TC_MX_CW * u + 4 * cw + rsub;
-            uint32_t p[8];
-            mx_decode_scaled(v[u], sbyte[u], p);
-            uint8_t* drow = dst + (c16 >> 2) * TC_A_BYTES + row * 128;
-            const int u0 = (c16 & 3) * 2;
-            *reinterpret_cast<uint4*>(drow + ((u0 ^ (row & 7)) << 4)) =
-                make_uint4(p[0], p[1], p[2], p[3]);
-            *reinterpret_cast<uint4*>(drow + (((u0 + 1) ^ (row & 7)) << 4)) =
-                make_uint4(p[4], p[5], p[6], p[7]);
-          }
+          // box j starts at scale block sb0 + 4 j of the 16-byte scale rows
+          mx_convert_box(w8 + j * TC_MX_BOX, conv + (size_t)cs * TC_MX_CONV, sc + sb0 + j * 4, 16,
+                         cw, lane);
           fence_proxy_async_smem();  // generic writes -> tensor-core reads
           __syncwarp();
           if (lane == 0) mbar_arrive(&cfull[cs]);
