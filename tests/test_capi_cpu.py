@@ -85,6 +85,7 @@ def test_rejected_calls_launch_nothing():
     assert capi.gate_up(0x1000, 0x2000, 0x3000, 0x4000, -1, 4, 2, 256, 8) == capi.WD_ERR_SHAPE
     assert capi.gate_up(0, 0x2000, 0x3000, 0x4000, 2, 4, 2, 256, 8) == capi.WD_ERR_NULL_POINTER
     assert L.wd_launch_count() == before
+    assert capi.launch_count() == before
 
 
 @pytest.mark.parametrize("args,code,msg", [

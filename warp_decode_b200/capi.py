@@ -203,6 +203,12 @@ def status_read(clear: bool = True) -> int:
     return int(v.value)
 
 
+def launch_count() -> int:
+    """Kernels the library has enqueued in this process (graph captures count
+    the launches they record; replays count none)."""
+    return int(lib().wd_launch_count())
+
+
 # ---------------------------------------------------------------------------
 # torch-tensor conveniences (device pointers + current stream)
 # ---------------------------------------------------------------------------
