@@ -73,6 +73,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
                    help="N > 1: all-reduce fused into the down kernel, or NCCL after it")
+    p.add_argument("--no-tp-full", action="store_true",
+                   help="skip the BASELINE configs[2] leg (full-width inter 1536 split over the N GPUs)")
     return p.parse_args()
 
 
@@ -82,13 +84,12 @@ def env_rank():
 
 
 def measured_peaks():
-    for p in (ROOT / "MEASURED_PEAKS.json", Path("/root/repo/MEASURED_PEAKS.json")):
-        try:
-            d = json.loads(p.read_text())
-            return float(d["hbm_gbs"]), "measured"
-        except Exception:
-            continue
-    return FALLBACK_HBM_GBS, "fallback"
+    """HBM copy bandwidth measured on this pool (MEASURED_PEAKS.json next to this file)."""
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 # ---------------------------------------------------------------------------
@@ -189,6 +190,82 @@ class L2Flush:
         torch.sum(self.b, dim=0, out=self.out)
 
 
+def fp32_reference_partial(x, w_gu, w_dn, ids, scale):
+    """This rank's FP32 partial [B, H] of the FFN by the FP32 formula of the
+    reference (tests/test_benchmark_reference.py:36-43): projections in
+    float64 rounded to FP32, silu(g)*u in FP32, h rounded to bf16 (the bf16
+    boundary at h), down projections in float64 rounded to FP32, times the
+    top-k weight, summed over the slots in FP32.  Plain torch on the device
+    (a checker, not the product): the sum over ranks of these partials is the
+    unsharded FFN, because silu(g)*u is elementwise in `inter`."""
+    import torch
+
+    B, K = ids.shape
+    I = w_gu.shape[1] // 2
+    flat = ids.reshape(-1).long()
+    xs = x.double().repeat_interleave(K, dim=0)                      # [B*K, H]
+    proj = torch.bmm(w_gu[flat].double(), xs.unsqueeze(-1)).squeeze(-1).float()
+    g, u = proj[:, :I], proj[:, I:]
+    h = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)          # [B*K, I]
+    p = torch.bmm(w_dn[flat].double(), h.double().unsqueeze(-1)).squeeze(-1).float()
+    p = p.view(B, K, -1) * scale.unsqueeze(-1)
+    y = torch.zeros_like(p[:, 0])
+    for s_ in range(K):
+        y = y + p[:, s_]
+    return y
+
+
+def check_parity(cases, e2e_call, nccl_call, w_gu, w_dn, world, fused, tol=1e-2):
+    """Outputs of the timed path against the FP32 reference (summed over the
+    ranks with NCCL when world > 1) at rtol = atol = tol; at world > 1 also
+    against the NCCL all-reduce path, the same bits on every rank, and the
+    same bits from both fused exchange shapes.  Returns the JSON record."""
+    import torch
+    import torch.distributed as dist
+
+    recs, ok_all = [], True
+    for c in cases:
+        y = e2e_call(c)
+        ref = fp32_reference_partial(c.x, w_gu, w_dn, c.ids, c.scale)
+        if world > 1:
+            dist.all_reduce(ref)
+        ref_bf = ref.to(torch.bfloat16).float()
+        yf = y.float()
+        d_ref = (yf - ref_bf).abs()
+        ok = bool((d_ref <= tol + tol * ref_bf.abs()).all().item())
+        rec = {"B": c.B, "max_abs_diff_vs_fp32_ref": float(d_ref.max().item())}
+        if world > 1:
+            yn = nccl_call(c).float()
+            d_n = (yf - yn).abs()
+            ok &= bool((d_n <= tol + tol * yn.abs()).all().item())
+            rec["max_abs_diff_vs_nccl"] = float(d_n.max().item())
+            gathered = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(gathered, y)
+            same = all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
+                       for g in gathered)
+            rec["identical_on_all_ranks"] = same
+            ok &= same
+            if fused is not None and fused.applies(c.B):
+                shapes_same = True
+                for mode in (1, 2):
+                    fused.set_exchange(mode)
+                    shapes_same &= torch.equal(e2e_call(c).view(torch.int16), y.view(torch.int16))
+                fused.set_exchange(0)
+                rec["exchange_shapes_identical"] = shapes_same
+                ok &= shapes_same
+        torch.cuda.synchronize()
+        flag = torch.tensor([1 if ok else 0], device=y.device)
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        rec["ok"] = bool(flag.item())
+        ok_all &= rec["ok"]
+        recs.append(rec)
+    return {"tol": {"rtol": tol, "atol": tol}, "reference": "FP32 formula of "
+            "tests/test_benchmark_reference.py:36-43 on the device (torch, float64 projections)"
+            + (", partials summed over the ranks" if world > 1 else ""),
+            "cases": recs, "ok": ok_all}
+
+
 def run_ours(args, rank, local_rank, world):
     import numpy as np
     import torch
@@ -260,16 +337,26 @@ def run_ours(args, rank, local_rank, world):
 
         fused = FusedAllReduce(H, max_tokens=64)
 
+    def nccl_call(c):
+        h = wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids)
+        part = wd.moe_down_3d_batched_partial(h, w_dn, c.ids, c.scale, c.B)
+        dist.all_reduce(part)
+        return part.to(torch.bfloat16)
+
     def e2e_call(c):
         if world == 1:
             return ffn(c.x, c.ids, c.scale)
         if fused is not None and fused.applies(c.B):
             # one launch (FFN + exchange) for B*topk <= 32, else gate_up + down
             return fused.ffn(c.x, w_gu, w_dn, c.ids, c.scale)
-        h = wd.moe_gate_up_3d_batched(c.x, w_gu, c.ids)
-        part = wd.moe_down_3d_batched_partial(h, w_dn, c.ids, c.scale, c.B)
-        dist.all_reduce(part)
-        return part.to(torch.bfloat16)
+        return nccl_call(c)
+
+    # Correctness of the timed path before timing it (every rank, same order).
+    parity = None
+    if not mx:
+        pcases = [cases[B] for B in (1, 8, 64) if B in cases] or [cases[batches[0]]]
+        parity = check_parity(pcases, e2e_call, nccl_call, w_gu, w_dn, world, fused)
+        torch.cuda.empty_cache()
 
     def capture(fn):
         """CUDA graph of one call, and how many of the library's kernels it holds."""
@@ -458,6 +545,14 @@ def run_ours(args, rank, local_rank, world):
                          ", x / topk_ids / topk_scale copied in from one pinned host buffer and y "
                          "copied out inside the timed window, L2 flushed before each call"}
 
+    tp_full = None
+    if args.workload == WORKLOAD and not args.no_extras and not args.no_tp_full:
+        for c in cases.values():
+            del c.g_e2e, c.g_gu, c.g_dn, c.g_split
+        torch.cuda.empty_cache()
+        tp_full = run_tp_full_leg(args, rank, local_rank, world, dev, flush, stream, cur,
+                                  fused, peak_gbs)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_timing(batches, H, I, E, K, cfg.routing, budget_s=args.cpu_seconds,
@@ -498,12 +593,15 @@ def run_ours(args, rank, local_rank, world):
             "impl": "ours",
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clock_rec,
             "gpu_launches": args.steps * sum(launches.values()),
+            "parity": parity,
             "sweep": sweep,
+            "tp_full": tp_full,
         }
         print(json.dumps(line), flush=True)
 
-    for c in cases.values():
-        del c.g_e2e, c.g_gu, c.g_dn, c.g_split
+    if tp_full is None:
+        for c in cases.values():
+            del c.g_e2e, c.g_gu, c.g_dn, c.g_split
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -511,6 +609,81 @@ def run_ours(args, rank, local_rank, world):
             fused.close()
         dist.destroy_process_group()
     return 0
+
+
+def run_tp_full_leg(args, rank, local_rank, world, dev, flush, stream, cur, fused, peak_gbs):
+    """BASELINE configs[2] after the headline: the full-width Qwen3-235B FFN
+    (hidden 4096, inter 1536, 128 experts, top-8) split over the N GPUs
+    (inter 1536 / N per GPU: TP1/2/4/8 = 1536/768/384/192), strong scaling,
+    at B in {1, 4, 16, 64}: cold us per call (L2 flushed, CUDA graph, events
+    on the launching stream, max over ranks) and the per-GPU HBM fraction on
+    that GPU's algorithmic bytes.  Reported beside the headline; it does not
+    change `value`."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from warp_decode_b200 import warp_decode as wd
+    from warp_decode_b200 import workloads as W
+
+    cfg = W.CONFIGS["qwen3_235b_full"]
+    H, E, K = cfg.hidden, cfg.E, cfg.topk
+    I = cfg.inter_full // world
+    w_gu, w_dn = W.make_device_weights(H, I, E, args.seed + 31 + 7919 * rank, device=dev)
+    reps = max(5, min(args.kernel_reps, 20))
+    rows = []
+    for B in cfg.batches:
+        x, ids, scale = W.make_device_activations(B, H, E, K, cfg.routing, args.seed + 500 + B,
+                                                  device=dev)
+        U = W.unique_experts(ids.cpu().numpy())
+        nbytes = W.algorithmic_bytes(U, B, H, I, K)["e2e"]
+
+        def call():
+            if world == 1:
+                return wd.moe_ffn_3d_batched(x, w_gu, w_dn, ids, scale)
+            if fused is not None and fused.applies(B):
+                return fused.ffn(x, w_gu, w_dn, ids, scale)
+            h = wd.moe_gate_up_3d_batched(x, w_gu, ids)
+            part = wd.moe_down_3d_batched_partial(h, w_dn, ids, scale, B)
+            dist.all_reduce(part)
+            return part.to(torch.bfloat16)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                call()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            call()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        ts = []
+        for _ in range(reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            g.replay()
+            b.record(cur)
+            ts.append((a, b))
+        torch.cuda.synchronize()
+        us = torch.tensor([float(np.mean([a.elapsed_time(b) for a, b in ts]) * 1000.0)],
+                          dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        us = float(us.item())
+        rows.append({"B": B, "us": round(us, 2), "unique_experts": U,
+                     "bytes_per_gpu": nbytes,
+                     "hbm_frac_per_gpu": round(nbytes / (us * 1e-6) / 1e9 / peak_gbs, 3)})
+        del g
+        torch.cuda.synchronize()
+    del w_gu, w_dn
+    torch.cuda.empty_cache()
+    return {"workload": f"qwen3_235b_full_tp{world}", "config": "BASELINE configs[2]",
+            "hidden": H, "inter_total": cfg.inter_full, "inter_per_gpu": I, "experts": E,
+            "topk": K, "scaling": "strong", "unit": UNIT,
+            "timing": "cold (L2 flushed), CUDA graph replay, CUDA events, mean of "
+                      f"{reps} calls, max over ranks",
+            "per_batch": rows, "mean_us": round(sum(r["us"] for r in rows) / len(rows), 3)}
 
 
 # ---------------------------------------------------------------------------

@@ -3,8 +3,11 @@
  *
  * This header is the drop-in boundary.  Every entry point takes plain device
  * pointers, sizes and a CUDA stream handle (passed as `void*`, i.e. the value
- * of a `cudaStream_t`; NULL means the legacy default stream).  Nothing here
- * allocates device memory, synchronises the stream, or depends on PyTorch.
+ * of a `cudaStream_t`; NULL means the legacy default stream).  No entry point
+ * synchronises the stream or depends on PyTorch, and only wd_tp_comm_create
+ * allocates device memory (the tensor-parallel exchange buffer); the kernels'
+ * other global memory is the caller's (h_buf, sync) or, for
+ * wd_moe_ffn_3d_batched_noalloc, a static array of the library.
  *
  * Reference interfaces replaced (Religious-J/warp_decode):
  *   wd_moe_gate_up_3d_batched  <- warp_decode::launch_moe_gate_up_3d_batched
@@ -184,7 +187,9 @@ WD_API int wd_set_down_path(int path);
  * one device.  NULL selects a counter owned by the library (one per device).
  * Calls that share a counter must not run at the same time (issue them on one
  * stream, or order them with events); give each concurrently used stream its
- * own.  After a call that raised WD_STATUS_WAIT_TIMEOUT, zero it again.
+ * own.  Every CTA of a call adds its one arrival before it waits, also in a
+ * call that ends in WD_STATUS_WAIT_TIMEOUT, so the counter stays a multiple
+ * of the grid size and is never reset.
  * Call once per device before capturing it in a CUDA graph (one-time device
  * setup).
  */
@@ -198,8 +203,9 @@ WD_API int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const voi
  * counterpart in the reference.  h and the grid-barrier counter live in a
  * file-scope static device array of the library (256 B + 128 KiB per
  * device); calls with B*topk*inter*2 > 131072 bytes return
- * WD_ERR_UNSUPPORTED.  The array's counter starts zeroed at module load and
- * needs no reset.  Every call on a device uses the same array, so calls that
+ * WD_ERR_UNSUPPORTED.  The array's counter starts zeroed at module load and,
+ * as for wd_moe_ffn_3d_batched, stays a multiple of the grid size after every
+ * call (a timed-out one included), so it needs no reset.  Every call on a device uses the same array, so calls that
  * overlap in time (other streams) race: serialise them.  The first call on a
  * device looks up the array's address (cudaGetSymbolAddress) and must not be
  * made while that device's stream is being captured.
@@ -249,7 +255,8 @@ WD_API int wd_set_ffn_path(int path);
  *      order).  Every rank must make the same sequence of calls (same B,
  *      shapes and order), like a collective, and enter each call within 2 s
  *      of each other.  Peers exchange rows as epoch-tagged packets through
- *      NVLink peer stores (no fences, no flags); a peer that does not arrive
+ *      NVLink peer stores (8-byte single-copy-atomic words, no fences, no
+ *      flags), one-shot or two-shot (wd_tp_comm_set_exchange); a peer that does not arrive
  *      within 2 s ends the wait with WD_STATUS_WAIT_TIMEOUT (the output is
  *      then zeros), never a hang.  Needs the tensor-core down kernel's shapes
  *      (inter <= 2048, E <= 1024) and B <= max_tokens per call chunk.
@@ -259,6 +266,15 @@ WD_API int wd_tp_comm_create(int world, int rank, int max_tokens, int hidden, vo
                              void* ipc_handle);
 WD_API int wd_tp_comm_open(void* comm, const void* ipc_handles);
 WD_API int wd_tp_comm_destroy(void* comm);
+/*
+ * Exchange shape of later calls on `comm` (no counterpart in the reference):
+ * 0 = by size (default: one-shot while a rank would send at most 512 KiB,
+ * B x hidden x 8 x (world - 1) bytes; WARP_DECODE_TP_TWO_SHOT_BYTES moves
+ * the threshold), 1 = one-shot (every rank sums every row), 2 = two-shot
+ * (row j summed by rank j * world / hidden, which sends the bf16 result to
+ * the others).  Both give the same bits.  Every rank must set the same mode.
+ */
+WD_API int wd_tp_comm_set_exchange(void* comm, int mode);
 WD_API int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down,
                                             const int32_t* topk_ids, const float* topk_scale,
                                             void* y_out, int B, int E, int topk, int hidden,

@@ -23,6 +23,7 @@ Usage:  python tests/golden/make_golden.py [--ref /path/to/reference]
 from __future__ import annotations
 
 import argparse
+import os
 import ast
 import importlib.util
 import json
@@ -120,8 +121,11 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("WARP_DECODE_REFERENCE"),
+                    help="checkout of Religious-J/warp_decode (default: $WARP_DECODE_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref or WARP_DECODE_REFERENCE must name the reference checkout")
     ref = Path(args.ref)
     torch.set_num_threads(8)
     ref_gate_up, ref_down = _load_reference_tests(ref)

@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 20, names
+    assert len(names) == 21, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n
@@ -147,3 +147,14 @@ def test_torch_binding_rejects_cpu_tensors():
         wd.moe_down_3d_batched(torch.zeros(2, 64, dtype=torch.bfloat16),
                                torch.zeros(4, 256, 64, dtype=torch.bfloat16), ids,
                                torch.zeros(1, 2), 1)
+
+
+def test_reference_import_surface():
+    """`from warp_decode import warp_decode as wd` (the reference's import,
+    tests/test_gate_up_correctness.py:16) gives this repository's extension."""
+    from warp_decode import warp_decode as wd
+    from warp_decode_b200 import warp_decode as wd_b200
+
+    assert wd is wd_b200
+    for name in ("moe_gate_up_3d_batched", "moe_down_3d_batched"):
+        assert callable(getattr(wd, name))

@@ -5,7 +5,8 @@ intermediate dimension of a Qwen3-235B-style FFN; the fused path
 (FusedAllReduce: epoch-tagged packets pushed to every rank by the single-launch
 FFN kernel at small B, by the tcgen05 down kernel above) must match the NCCL
 path and the unsharded FP32 oracle (rtol = atol = 1e-2), give
-bitwise-identical outputs on both ranks, keep its epochs in step when the two
+bitwise-identical outputs on both ranks and in both exchange shapes
+(one-shot and two-shot), keep its epochs in step when the two
 kernels take turns on one communicator, survive CUDA-graph replay (epochs
 advance), and end a wait whose peer never arrives with WD_STATUS_WAIT_TIMEOUT
 within the 2 s bound instead of hanging.  NVLS is off (NCCL_NVLS_ENABLE=0).
@@ -66,6 +67,17 @@ def _worker(rank, port, out_dir):
             xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
             h_ref = O.gate_up(xb, touched(w_gu), ids_h)
             res[f"ref_{B}"] = O.down(h_ref, touched(w_dn), ids_h, scale.cpu().numpy())
+    # Both exchange shapes, forced, on both kernels: the same bits.
+    for mode in (1, 2):
+        fused.set_exchange(mode)
+        for B in (1, 8, 64):
+            dist.barrier(device_ids=[rank])
+            x, ids, scale = W.make_device_activations(B, H, E, K, "uniform", 900 + B, device=dev)
+            y = moe_fused(x, ids, scale)
+            torch.cuda.synchronize()
+            res[f"mode{mode}_{B}"] = y.cpu().view(torch.int16).numpy()
+            res[f"mode{mode}_status_{B}"] = wd.status(True, rank)
+    fused.set_exchange(0)
     # The single-launch FFN (B = 1) and the tcgen05 down kernel (B = 4) take
     # turns on one communicator: every call advances every epoch entry.  The
     # ranks enter every fused call within the 2 s wait bound of each other
@@ -145,6 +157,11 @@ def test_fused_allreduce_two_gpus(tmp_path):
         assert ok, f"B={B}: fused vs oracle max |diff| {d}"
         ok, d = bf16_close(r0[f"nccl_{B}"].view(np.uint16), r0[f"ref_{B}"], 1e-2, 1e-2)
         assert ok, f"B={B}: NCCL path vs oracle max |diff| {d}"
+        for r in (r0, r1):
+            for mode in (1, 2):
+                assert r[f"mode{mode}_status_{B}"] == 0
+                assert np.array_equal(r[f"mode{mode}_{B}"].view(np.uint16), f0), \
+                    f"B={B}: exchange shape {mode} changed the bits"
     for r in (r0, r1):
         for B in (2, 16):
             g = r[f"graph_{B}"]

@@ -1,7 +1,7 @@
 """ctypes binding of the C ABI in ``include/warp_decode.h``.
 
-This is the binding a non-PyTorch host would write; the
-tests use it to drive the kernels through the exact C entry points.  Pointers
+This is the binding a non-PyTorch host would write for the C ABI; the tests
+use it to drive the kernels through the exact C entry points.  Pointers
 are plain integers (device addresses), streams are ``cudaStream_t`` values.
 """
 from __future__ import annotations
@@ -42,6 +42,7 @@ _SIGS = {
     "wd_tp_comm_create": (_I, [_I, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p), _P]),
     "wd_tp_comm_open": (_I, [_P, _P]),
     "wd_tp_comm_destroy": (_I, [_P]),
+    "wd_tp_comm_set_exchange": (_I, [_P, _I]),
     "wd_moe_down_3d_batched_allreduce": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
                                               _P]),
     "wd_moe_ffn_3d_batched": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
@@ -166,6 +167,15 @@ def tp_comm_open(comm: int, handles: bytes) -> None:
 
 def tp_comm_destroy(comm: int) -> None:
     check(lib().wd_tp_comm_destroy(comm))
+
+
+# Values of tp_comm_set_exchange.
+EXCHANGE_AUTO, EXCHANGE_ONE_SHOT, EXCHANGE_TWO_SHOT = 0, 1, 2
+
+
+def tp_comm_set_exchange(comm: int, mode: int) -> None:
+    """Exchange shape of later fused all-reduce calls (EXCHANGE_AUTO / _ONE_SHOT / _TWO_SHOT)."""
+    check(lib().wd_tp_comm_set_exchange(comm, int(mode)))
 
 
 def torch_ffn_allreduce(x, w_gu, w_dn, ids, scale, comm):

@@ -56,35 +56,115 @@ constexpr int DTC_MX_THREADS = DTC_THREADS + DTC_MX_CW * 32;
 constexpr int DTC_MX_BOX = DTC_M * 128;          // E4M3 box: 128 rows x 128 K (bytes)
 constexpr int DTC_MX_NMAX = 16;                  // tokens per MXFP8 launch
 
-// Fused one-shot all-reduce over the ranks of a tensor-parallel group (one
-// process per GPU, peer memory opened through CUDA IPC).  Every rank's
-// buffer holds [2 slots][world][max_tokens][H] packets of 8 bytes: the FP32
-// partial and the epoch of the call that wrote it, stored together by one
-// 8-byte store, so a reader that sees the epoch sees the value (no fences,
-// no separate flags).  epochs[] counts this rank's calls: CTA c of a call
-// reads epochs[c] and at the end writes the new count to epochs[c],
-// epochs[c + grid], ..., so every entry advances by one per call whatever grid
-// the kernel used (the single-launch FFN and this kernel partition the rows
+// Fused all-reduce over the ranks of a tensor-parallel group (one process per
+// GPU, peer memory opened through CUDA IPC).  Every rank's buffer holds
+// [2 slots][world][max_tokens][H] packets of 8 bytes: the FP32 value in the
+// low half and the epoch of the call that wrote it in the high half, stored
+// and loaded as ONE 64-bit access (single-copy atomic), so a reader that sees
+// the epoch sees the value that came with it (no fences, no separate flags).
+// epochs[] counts this rank's calls: CTA c of a call reads epochs[c] and at
+// the end writes the new count to epochs[c], epochs[c + grid], ..., so every
+// entry advances by one per call whatever grid the kernel used (the
+// single-launch FFN and the tensor-core down kernel partition the rows
 // differently; a packet left by either never carries a current epoch).
 // slot = epoch & 1 keeps a rank that is one call ahead off the slot still
-// being read.
+// being read: a rank finishes call k + 1 only after hearing from every peer
+// in call k + 1, and a peer's call k + 1 starts after its call k has ended.
+//
+// Two exchange shapes, the same result bits (every row is summed over the
+// ranks' FP32 partials in rank order, then rounded to bf16 once):
+//  * one-shot: every rank pushes its partial of every row to every rank and
+//    sums all ranks' packets itself (one NVLink latency, B*H*8*(world-1)
+//    bytes sent per rank);
+//  * two-shot: row j is owned by rank j*world/H.  A rank pushes its partial
+//    of a row to the owner only; the owner sums the packets in rank order
+//    and pushes the bf16 result (as an FP32 packet) to the other ranks,
+//    which take it from their own buffer at [owner][t][j] (two latencies,
+//    about 2*B*H*8*(world-1)/world bytes per rank).
+// Every push of a call precedes every wait of the same thread, owners sum
+// before they gather, and all waits poll local memory only.
 constexpr int TP_MAX_WORLD = 8;
 struct TpArgs {
   int world;                        // <= 1: no fused all-reduce
   int rank;
   int max_tokens, max_ctas;
-  uint2* recv[TP_MAX_WORLD];        // packet buffers of every rank (peer pointers)
+  int two_shot;                     // exchange shape (see above)
+  unsigned long long* recv[TP_MAX_WORLD];  // packet buffers of every rank (peer pointers)
   uint32_t* epochs;                 // this rank's per-CTA call counters
 };
 
-__device__ __forceinline__ void st_volatile_u2(uint2* p, uint32_t a, uint32_t b) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+__device__ __forceinline__ void tp_put(unsigned long long* p, float v, uint32_t ep) {
+  const unsigned long long w =
+      ((unsigned long long)ep << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint2 ld_volatile_u2(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ unsigned long long tp_peek(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
+// The value of the packet at p once it carries epoch ep; false if it did not
+// arrive within WD_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool tp_take(const unsigned long long* p, uint32_t ep, float& v) {
+  unsigned long long w = tp_peek(p);
+  if ((uint32_t)(w >> 32) != ep) {
+    const uint64_t t0 = globaltimer_ns();
+    do {
+      w = tp_peek(p);
+      if ((uint32_t)(w >> 32) != ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) return false;
+    } while ((uint32_t)(w >> 32) != ep);
+  }
+  v = __uint_as_float((uint32_t)w);
+  return true;
+}
+
+// One call's view of the exchange.
+struct TpCall {
+  const TpArgs& tp;
+  uint32_t ep;  // this call's epoch
+  int H;
+  __device__ unsigned long long* at(int dst, int src, int t, int row) const {
+    return tp.recv[dst] +
+           (((size_t)((int)(ep & 1u) * tp.world + src) * tp.max_tokens + t) * H + row);
+  }
+  // The rank that sums `row` (every rank sums every row one-shot).
+  __device__ int owner(int row) const {
+    return tp.two_shot ? (int)(((long long)row * tp.world) / H) : tp.rank;
+  }
+  __device__ bool sums(int row) const { return owner(row) == tp.rank; }
+  // This rank's FP32 partial of (t, row) to the rank(s) that sum it.
+  __device__ void push(int t, int row, float v) const {
+    if (tp.two_shot) {
+      tp_put(at(owner(row), tp.rank, t, row), v, ep);
+    } else {
+      for (int r = 0; r < tp.world; ++r) tp_put(at(r, tp.rank, t, row), v, ep);
+    }
+  }
+  // Sum of every rank's partial of (t, row) in rank order (a row this rank
+  // sums); two-shot also sends the bf16 result to the other ranks.
+  __device__ bool reduce(int t, int row, __nv_bfloat16& y) const {
+    float s = 0.f;
+    for (int r = 0; r < tp.world; ++r) {
+      float v;
+      if (!tp_take(at(tp.rank, r, t, row), ep, v)) return false;
+      s += v;
+    }
+    y = __float2bfloat16_rn(s);
+    if (tp.two_shot) {
+      const float yf = __bfloat162float(y);
+      for (int r = 0; r < tp.world; ++r)
+        if (r != tp.rank) tp_put(at(r, tp.rank, t, row), yf, ep);
+    }
+    return true;
+  }
+  // Two-shot: the owner's result of (t, row), a row this rank does not sum.
+  __device__ bool gather(int t, int row, __nv_bfloat16& y) const {
+    float v;
+    if (!tp_take(at(tp.rank, owner(row), t, row), ep, v)) return false;
+    y = __float2bfloat16_rn(v);
+    return true;
+  }
+};
 
 struct DownTcArgs {
   const __nv_bfloat16* h;  // [B*K, I]
@@ -564,12 +644,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   const int hi = ((rank + 1) * (DTC_M / 4) / CL) * 4;
   const int q4 = (hi - lo) / 4;
   const bool tp = kTP && a.tp.world > 1;
-  const uint32_t ep = tp_ep;  // this call's epoch (read at kernel start)
-  const int slot = (int)(ep & 1u);
-  auto recv_at = [&](uint2* buf, int src, int t, int row) {
-    return buf + (((size_t)(slot * a.tp.world + src) * a.tp.max_tokens + t) * a.H + row);
-  };
-  bool tp_ok = true;
+  const TpCall xc{a.tp, tp_ep, a.H};  // this call's exchange (tp only)
   for (int i = threadIdx.x; i < a.B * q4; i += blockDim.x) {
     const int t = i / q4, jj = lo + 4 * (i - t * q4);
     const float* src = &Y[t * DTC_M + jj];
@@ -591,45 +666,10 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
     }
     const float v[4] = {acc.x, acc.y, acc.z, acc.w};
     if constexpr (kTP) if (tp) {
-      // Push (value, epoch) packets of this rank's rows to every rank, then
-      // collect every rank's packets of the same rows and add them in rank
-      // order.  A packet that does not arrive within the bound counts as 0
-      // and raises WD_STATUS_WAIT_TIMEOUT.
-      for (int r = 0; r < a.tp.world; ++r) {
-        uint2* dst = recv_at(a.tp.recv[r], a.tp.rank, t, j0 + jj);
+      // This rank's partials of the rows go out first (no wait in between).
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (j0 + jj + u < a.H) st_volatile_u2(dst + u, __float_as_uint(v[u]), ep);
-      }
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      uint2* mine = a.tp.recv[a.tp.rank];
-      for (int r = 0; r < a.tp.world; ++r) {
-        const uint2* p = recv_at(mine, r, t, j0 + jj);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (j0 + jj + u >= a.H || !tp_ok) continue;
-          uint2 pk = ld_volatile_u2(p + u);
-          if (pk.y != ep) {
-            const uint64_t t0 = globaltimer_ns();
-            do {
-              pk = ld_volatile_u2(p + u);
-              if (pk.y != ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
-                raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-                tp_ok = false;
-                break;
-              }
-            } while (pk.y != ep);
-          }
-          if (tp_ok) sum[u] += __uint_as_float(pk.x);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = j0 + jj + u;
-        if (row < a.H)
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.H + row] =
-              __float2bfloat16_rn(tp_ok ? sum[u] : 0.f);
-      }
+      for (int u = 0; u < 4; ++u)
+        if (j0 + jj + u < a.H) xc.push(t, j0 + jj + u, v[u]);
       continue;
     }
 #pragma unroll
@@ -644,8 +684,30 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
       }
     }
   }
+  if constexpr (kTP) if (tp) {
+    // Rows this rank sums (all of them one-shot), then (two-shot) the rows
+    // whose owner sends the result.  A packet that does not arrive within
+    // the bound gives a zero row and raises WD_STATUS_WAIT_TIMEOUT.
+    bool tp_ok = true;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.out);
+    for (int pass = 0; pass < (a.tp.two_shot ? 2 : 1); ++pass) {
+      for (int i = threadIdx.x; i < a.B * (hi - lo); i += blockDim.x) {
+        const int t = i / (hi - lo), row = j0 + lo + (i - t * (hi - lo));
+        if (row >= a.H || xc.sums(row) != (pass == 0)) continue;
+        __nv_bfloat16 yv = __float2bfloat16_rn(0.f);
+        if (tp_ok) {
+          tp_ok = pass == 0 ? xc.reduce(t, row, yv) : xc.gather(t, row, yv);
+          if (!tp_ok) {
+            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            yv = __float2bfloat16_rn(0.f);
+          }
+        }
+        y[(size_t)t * a.H + row] = yv;
+      }
+    }
+  }
   if (tp && threadIdx.x == 0)
-    for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += (int)gridDim.x) a.tp.epochs[c2] = ep;
+    for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += (int)gridDim.x) a.tp.epochs[c2] = tp_ep;
   if (CL > 1) cluster_sync();  // no CTA leaves while a peer may read its tile
 }
 

@@ -28,10 +28,10 @@
 //    token; per-warp FP32 tiles summed in a fixed order (deterministic, no
 //    atomics on y).
 //  * Tensor parallelism (kTP): the CTA's FP32 rows are this rank's partial
-//    sums; they go to every rank as (value, epoch) packets over NVLink peer
-//    stores and the CTA adds every rank's packets of its rows in rank order
-//    (the exchange of the tcgen05 down kernel, TpArgs): y is the all-reduced
-//    bf16 output, identical bits on every rank, with no other launch.
+//    sums; they are all-reduced over NVLink peer stores of 8-byte (value,
+//    epoch) packets, one-shot or two-shot (the exchange of the tcgen05 down
+//    kernel, TpArgs / TpCall): y is the all-reduced bf16 output, identical
+//    bits on every rank, with no other launch.
 //  * Short code on the launch's critical path: after an L2 flush the kernel's
 //    instructions come from DRAM, and each taken branch into code not yet
 //    fetched costs about a DRAM latency.  Routing compiles only the
@@ -453,49 +453,38 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
     return;
   }
   if constexpr (kTP) {
-    // Push this rank's partial rows to every rank, then add every rank's
-    // packets of the same rows in rank order (bounded waits: a packet that
-    // does not arrive within 2 s counts as 0 and raises WD_STATUS_WAIT_TIMEOUT).
-    const TpArgs& tp = a.tp;
-    const int slot = (int)(tp_ep & 1u);
-    auto recv_at = [&](uint2* buf, int src, int t, int row) {
-      return buf + (((size_t)(slot * tp.world + src) * tp.max_tokens + t) * H + row);
-    };
+    // This rank's partial rows go out first (TpCall: one-shot or two-shot);
+    // then the rows this rank sums, in rank order, and (two-shot) the rows
+    // whose owner sends the result.  A packet that does not arrive within
+    // 2 s gives a zero row and raises WD_STATUS_WAIT_TIMEOUT.
+    const TpCall xc{a.tp, tp_ep, a.H};
     for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
       const int b = i / nrows;
       const int lr = i - b * nrows;
       float v = 0.f;
 #pragma unroll
       for (int w = 0; w < NCW; ++w) v += tiles[(size_t)w * tile + b * a.rows_max + lr];
-      for (int r = 0; r < tp.world; ++r)
-        st_volatile_u2(recv_at(tp.recv[r], tp.rank, b, r0 + lr), __float_as_uint(v), tp_ep);
+      xc.push(b, r0 + lr, v);
     }
     bool ok = true;
-    for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
-      const int b = i / nrows;
-      const int lr = i - b * nrows;
-      float sum = 0.f;
-      for (int r = 0; r < tp.world && ok; ++r) {
-        const uint2* pk = recv_at(tp.recv[tp.rank], r, b, r0 + lr);
-        uint2 v = ld_volatile_u2(pk);
-        if (v.y != tp_ep) {
-          const uint64_t t0 = globaltimer_ns();
-          do {
-            v = ld_volatile_u2(pk);
-            if (v.y != tp_ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
-              raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-              ok = false;
-              break;
-            }
-          } while (v.y != tp_ep);
+    for (int pass = 0; pass < (a.tp.two_shot ? 2 : 1); ++pass) {
+      for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
+        const int b = i / nrows;
+        const int row = r0 + (i - b * nrows);
+        if (xc.sums(row) != (pass == 0)) continue;
+        __nv_bfloat16 yv = __float2bfloat16_rn(0.f);
+        if (ok) {
+          ok = pass == 0 ? xc.reduce(b, row, yv) : xc.gather(b, row, yv);
+          if (!ok) {
+            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            yv = __float2bfloat16_rn(0.f);
+          }
         }
-        if (ok) sum += __uint_as_float(v.x);
+        reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)b * H + row] = yv;
       }
-      reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)b * H + r0 + lr] =
-          __float2bfloat16_rn(ok ? sum : 0.f);
     }
     if (threadIdx.x == 0)
-      for (int c2 = (int)blockIdx.x; c2 < tp.max_ctas; c2 += G) tp.epochs[c2] = tp_ep;
+      for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += G) a.tp.epochs[c2] = tp_ep;
   } else {
     // y = sum of the 8 warp tiles in a fixed order.
     for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {

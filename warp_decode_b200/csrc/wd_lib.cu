@@ -1109,21 +1109,36 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
 struct TpComm {
   int device = -1;
   int world = 0, rank = 0, max_tokens = 0, hidden = 0, max_ctas = 0;
+  int exchange = 0;               // 0 = by size, 1 = one-shot, 2 = two-shot
   void* block = nullptr;          // [2][world][max_tokens][hidden] 8-byte packets
   size_t recv_bytes = 0;
   uint32_t* epochs = nullptr;     // [max_ctas], local only
   void* peer[wdb::TP_MAX_WORLD] = {};  // opened IPC mappings (nullptr for self)
 };
 
-wdb::TpArgs make_tp_args(const TpComm* c) {
+// Bytes a rank sends one-shot (B x hidden x 8 x (world - 1)) above which the
+// automatic choice takes the two-shot exchange, which sends about
+// 2 / world of that at the price of a second NVLink latency.
+// WARP_DECODE_TP_TWO_SHOT_BYTES overrides it.
+size_t tp_two_shot_bytes() {
+  static const size_t v = [] {
+    const char* e = std::getenv("WARP_DECODE_TP_TWO_SHOT_BYTES");
+    return e && *e ? (size_t)std::strtoull(e, nullptr, 10) : (size_t)(512u << 10);
+  }();
+  return v;
+}
+
+wdb::TpArgs make_tp_args(const TpComm* c, int B) {
   wdb::TpArgs tp = {};
   tp.world = c->world;
   tp.rank = c->rank;
   tp.max_tokens = c->max_tokens;
   tp.max_ctas = c->max_ctas;
   tp.epochs = c->epochs;
+  const size_t one_shot = (size_t)B * c->hidden * 8 * (c->world - 1);
+  tp.two_shot = c->exchange == 2 || (c->exchange == 0 && one_shot > tp_two_shot_bytes()) ? 1 : 0;
   for (int r = 0; r < c->world; ++r)
-    tp.recv[r] = static_cast<uint2*>(r == c->rank ? c->block : c->peer[r]);
+    tp.recv[r] = static_cast<unsigned long long*>(r == c->rank ? c->block : c->peer[r]);
   return tp;
 }
 
@@ -1364,6 +1379,16 @@ int wd_tp_comm_open(void* comm, const void* ipc_handles) {
   return WD_OK;
 }
 
+int wd_tp_comm_set_exchange(void* comm, int mode) {
+  g_last_error.clear();
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (!c) return fail(WD_ERR_NULL_POINTER, "comm is NULL");
+  if (mode < 0 || mode > 2)
+    return fail(WD_ERR_SHAPE, "mode must be 0 (by size), 1 (one-shot) or 2 (two-shot)");
+  c->exchange = mode;
+  return WD_OK;
+}
+
 int wd_tp_comm_destroy(void* comm) {
   g_last_error.clear();
   TpComm* c = static_cast<TpComm*>(comm);
@@ -1399,11 +1424,11 @@ int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down, const in
   if (E > wdb::MAX_DEDUP_E || inter > wdb::DTC_MAXKC * wdb::DTC_BK ||
       (hidden + wdb::DTC_M - 1) / wdb::DTC_M > dev->sm_count)
     return fail(WD_ERR_UNSUPPORTED, "shape outside the tensor-core down kernel (inter <= 2048)");
-  const wdb::TpArgs tp = make_tp_args(c);
   const int tb = std::min(std::max(1, wdb::MAX_SLOTS / topk), std::min(64, c->max_tokens));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int b0 = 0; b0 < B; b0 += tb) {
     const int bn = std::min(tb, B - b0);
+    const wdb::TpArgs tp = make_tp_args(c, bn);
     rc = down_tc_launch(dev, reinterpret_cast<const __nv_bfloat16*>(h) + (size_t)b0 * topk * inter,
                         w_down, topk_ids + (size_t)b0 * topk, topk_scale + (size_t)b0 * topk,
                         reinterpret_cast<__nv_bfloat16*>(y_out) + (size_t)b0 * hidden, 0, bn, E,
@@ -1443,7 +1468,7 @@ int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up, const 
       ffn_plan(dev, B, E, topk, hidden, inter,
                fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan) &&
       plan.grid <= c->max_ctas) {
-    const wdb::TpArgs tp = make_tp_args(c);
+    const wdb::TpArgs tp = make_tp_args(c, B);
     return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
                       sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, 0, B, E,
                       topk, hidden, inter, status, reinterpret_cast<cudaStream_t>(stream), &tp);

@@ -11,9 +11,9 @@ benchmark/bench.py:307-310 of Religious-J/warp_decode divides inter by
 * gate_up needs no communication; down produces an FP32 partial [B, hidden]
   (no bf16 rounding before the sum), followed by ONE all-reduce (NCCL over
   NVLink on GPUs) and a single bf16 rounding -- or, with FusedAllReduce, the
-  down kernel itself pushes its FP32 rows to every rank over NVLink as
-  epoch-tagged 8-byte packets and sums the ranks' rows in rank order (one
-  kernel, no NCCL launch, no fences).
+  down kernel itself exchanges its FP32 rows over NVLink as epoch-tagged
+  8-byte packets (one-shot at small sizes, two-shot above) and sums the
+  ranks' rows in rank order (one kernel, no NCCL launch, no fences).
 
 Because silu(gate)*up is elementwise in the intermediate dimension and down
 is linear in it, sum_r down_r(gate_up_r(x)) equals the unsharded FFN up to
@@ -89,19 +89,24 @@ class FusedAllReduce:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.hidden = hidden
+        self.max_tokens = max_tokens
         self.comm, handle = capi.tp_comm_create(self.world, self.rank, max_tokens, hidden)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         capi.tp_comm_open(self.comm, b"".join(handles))
 
-    # The one-shot exchange pushes B x hidden x 8 bytes to each of world - 1
-    # peers per call; above this many bytes per rank NCCL's algorithms move
-    # less data and win (measured on 8 x B200: fused ahead up to B = 8 at
-    # world 8, at every B up to 64 at world 2).
-    MAX_PUSH_BYTES = 2 << 20
-
     def applies(self, B: int) -> bool:
-        return B * self.hidden * 8 * (self.world - 1) <= self.MAX_PUSH_BYTES
+        """Whether a call of B tokens fits the communicator (B <= max_tokens).
+
+        The exchange shape follows the size (one-shot up to 512 KiB sent per
+        rank, two-shot above, which sends about 2/world of the one-shot bytes),
+        so the fused path replaces NCCL at every batch the buffer holds.
+        """
+        return 1 <= B <= self.max_tokens
+
+    def set_exchange(self, mode: int) -> None:
+        """Force the exchange shape: 0 by size, 1 one-shot, 2 two-shot (same bits)."""
+        self.capi.tp_comm_set_exchange(self.comm, mode)
 
     def down(self, h, w, ids, scale):
         return self.capi.torch_down_allreduce(h, w, ids, scale, self.comm)
