@@ -454,12 +454,26 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
   // more than 64 tokens, sends the launch to the ordered warp pass.
   const int ntok = n / K;
   bool slow = ntok > 64;
-  if (!slow) {
+  if (!slow && (32 % K) == 0) {
+    // K divides 32: a warp's 32 consecutive slots are whole tokens, so one
+    // match_any on (expert, token) finds a repeat inside a token.  The mask
+    // bit goes in with a 32-bit shared atomic on the word holding it.
+    for (int c = warp * 32; c < n; c += nt) {
+      const int i = c + lane;
+      const bool v = i < n;
+      const int key = v ? (r.ids[i] < 0 ? E : r.ids[i]) : 0;
+      const int t = i / K;
+      const unsigned m = __match_any_sync(0xffffffffu, v ? key * 64 + t : -1 - lane);
+      slow |= __popc(m) > 1;
+      if (v)
+        atomicOr(reinterpret_cast<unsigned*>(&r.mask[key]) + (t >> 5), 1u << (t & 31));
+    }
+  } else if (!slow) {
     for (int i = tid; i < n; i += nt) {
       const int key = r.ids[i] < 0 ? E : r.ids[i];
       const int t = i / K;
       for (int j = t * K; j < i; ++j) slow |= ((r.ids[j] < 0 ? E : r.ids[j]) == key);
-      atomicOr(&r.mask[key], 1ull << t);
+      atomicOr(reinterpret_cast<unsigned*>(&r.mask[key]) + (t >> 5), 1u << (t & 31));
     }
   }
   slow = __syncthreads_or(slow);
