@@ -268,11 +268,11 @@ WD_API int wd_tp_comm_open(void* comm, const void* ipc_handles);
 WD_API int wd_tp_comm_destroy(void* comm);
 /*
  * Exchange shape of later calls on `comm` (no counterpart in the reference):
- * 0 = by size (default: one-shot while a rank would send at most 512 KiB,
- * B x hidden x 8 x (world - 1) bytes; WARP_DECODE_TP_TWO_SHOT_BYTES moves
- * the threshold), 1 = one-shot (every rank sums every row), 2 = two-shot
- * (row j summed by rank j * world / hidden, which sends the bf16 result to
- * the others).  Both give the same bits.  Every rank must set the same mode.
+ * 0 = by size (default: one-shot with two ranks, and while a rank would
+ * send at most 512 KiB, B x hidden x 8 x (world - 1) bytes;
+ * WARP_DECODE_TP_TWO_SHOT_BYTES moves the threshold), 1 = one-shot (every rank sums every row), 2 = two-shot
+ * (row j summed by rank (j / 4) % world, which sends the bf16 result to the
+ * others).  Both give the same bits.  Every rank must set the same mode.
  */
 WD_API int wd_tp_comm_set_exchange(void* comm, int mode);
 WD_API int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down,

@@ -76,7 +76,7 @@ constexpr int DTC_MX_NMAX = 16;                  // tokens per MXFP8 launch
 //  * one-shot: every rank pushes its partial of every row to every rank and
 //    sums all ranks' packets itself (one NVLink latency, B*H*8*(world-1)
 //    bytes sent per rank);
-//  * two-shot: row j is owned by rank j*world/H.  A rank pushes its partial
+//  * two-shot: row j is owned by rank (j/4) % world.  A rank pushes its partial
 //    of a row to the owner only; the owner sums the packets in rank order
 //    and pushes the bf16 result (as an FP32 packet) to the other ranks,
 //    which take it from their own buffer at [owner][t][j] (two latencies,
@@ -132,10 +132,10 @@ struct TpCall {
     return tp.recv[dst] +
            (((size_t)((int)(ep & 1u) * tp.world + src) * tp.max_tokens + t) * H + row);
   }
-  // The rank that sums `row` (every rank sums every row one-shot).
-  __device__ int owner(int row) const {
-    return tp.two_shot ? (int)(((long long)row * tp.world) / H) : tp.rank;
-  }
+  // The rank that sums `row` (every rank sums every row one-shot).  Two-shot:
+  // four-row units dealt round robin, so every CTA sums about 1/world of its
+  // rows on every rank (no rank's CTAs do all the summing).
+  __device__ int owner(int row) const { return tp.two_shot ? (row >> 2) % tp.world : tp.rank; }
   __device__ bool sums(int row) const { return owner(row) == tp.rank; }
   // This rank's FP32 partial of (t, row) to the rank(s) that sum it.
   __device__ void push(int t, int row, float v) const {
@@ -145,14 +145,35 @@ struct TpCall {
       for (int r = 0; r < tp.world; ++r) tp_put(at(r, tp.rank, t, row), v, ep);
     }
   }
+  // The value of the packet at p, given a first reading w, once it carries
+  // this call's epoch; false if it did not arrive within WD_WAIT_LIMIT_NS.
+  __device__ bool settle(const unsigned long long* p, unsigned long long w, float& v) const {
+    if ((uint32_t)(w >> 32) != ep) {
+      const uint64_t t0 = globaltimer_ns();
+      do {
+        w = tp_peek(p);
+        if ((uint32_t)(w >> 32) != ep && globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) return false;
+      } while ((uint32_t)(w >> 32) != ep);
+    }
+    v = __uint_as_float((uint32_t)w);
+    return true;
+  }
   // Sum of every rank's partial of (t, row) in rank order (a row this rank
-  // sums); two-shot also sends the bf16 result to the other ranks.
+  // sums; the ranks' packets are read together, then any late one polled);
+  // two-shot also sends the bf16 result to the other ranks.
   __device__ bool reduce(int t, int row, __nv_bfloat16& y) const {
+    unsigned long long w[TP_MAX_WORLD];
+#pragma unroll
+    for (int r = 0; r < TP_MAX_WORLD; ++r)
+      if (r < tp.world) w[r] = tp_peek(at(tp.rank, r, t, row));
     float s = 0.f;
-    for (int r = 0; r < tp.world; ++r) {
-      float v;
-      if (!tp_take(at(tp.rank, r, t, row), ep, v)) return false;
-      s += v;
+#pragma unroll
+    for (int r = 0; r < TP_MAX_WORLD; ++r) {
+      if (r < tp.world) {
+        float v;
+        if (!settle(at(tp.rank, r, t, row), w[r], v)) return false;
+        s += v;
+      }
     }
     y = __float2bfloat16_rn(s);
     if (tp.two_shot) {
@@ -162,14 +183,60 @@ struct TpCall {
     }
     return true;
   }
-  // Two-shot: the owner's result of (t, row), a row this rank does not sum.
-  __device__ bool gather(int t, int row, __nv_bfloat16& y) const {
-    float v;
-    if (!tp_take(at(tp.rank, owner(row), t, row), ep, v)) return false;
-    y = __float2bfloat16_rn(v);
-    return true;
-  }
 };
+
+// This rank's output rows of the call after its pushes: entry i (i =
+// threadIdx.x, + blockDim.x, ... < n) is (t, row) = entry(i), skipped where
+// entry() returns false.  First the rows this rank sums (all one-shot), then
+// (two-shot) the other rows from their owners, eight entries per thread in
+// flight.  A packet that does not arrive within the bound gives a zero and
+// raises WD_STATUS_WAIT_TIMEOUT; returns false then.
+template <class Entry>
+__device__ inline bool tp_collect(const TpCall& xc, int n, Entry entry, __nv_bfloat16* y,
+                                  uint32_t* status) {
+  bool ok = true;
+  const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int t, row;
+    if (!entry(i, t, row) || !xc.sums(row)) continue;
+    __nv_bfloat16 yv = zero;
+    if (ok && !xc.reduce(t, row, yv)) {
+      ok = false;
+      yv = zero;
+      raise_status(status, WD_STATUS_WAIT_TIMEOUT);
+    }
+    y[(size_t)t * xc.H + row] = yv;
+  }
+  if (!xc.tp.two_shot) return ok;
+  constexpr int GB = 8;
+  for (int i0 = threadIdx.x; i0 < n; i0 += GB * (int)blockDim.x) {
+    int tt[GB], rr[GB];
+    bool take[GB];
+    unsigned long long w[GB];
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = i0 + j * (int)blockDim.x;
+      take[j] = i < n && entry(i, tt[j], rr[j]) && !xc.sums(rr[j]);
+      if (take[j]) w[j] = tp_peek(xc.at(xc.tp.rank, xc.owner(rr[j]), tt[j], rr[j]));
+    }
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      if (!take[j]) continue;
+      __nv_bfloat16 yv = zero;
+      float v;
+      if (ok) {
+        if (xc.settle(xc.at(xc.tp.rank, xc.owner(rr[j]), tt[j], rr[j]), w[j], v)) {
+          yv = __float2bfloat16_rn(v);
+        } else {
+          ok = false;
+          raise_status(status, WD_STATUS_WAIT_TIMEOUT);
+        }
+      }
+      y[(size_t)tt[j] * xc.H + rr[j]] = yv;
+    }
+  }
+  return ok;
+}
 
 struct DownTcArgs {
   const __nv_bfloat16* h;  // [B*K, I]
@@ -690,26 +757,12 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
     }
   }
   if constexpr (kTP) if (tp) {
-    // Rows this rank sums (all of them one-shot), then (two-shot) the rows
-    // whose owner sends the result.  A packet that does not arrive within
-    // the bound gives a zero row and raises WD_STATUS_WAIT_TIMEOUT.
-    bool tp_ok = true;
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.out);
-    for (int pass = 0; pass < (a.tp.two_shot ? 2 : 1); ++pass) {
-      for (int i = threadIdx.x; i < a.B * (hi - lo); i += blockDim.x) {
-        const int t = i / (hi - lo), row = j0 + lo + (i - t * (hi - lo));
-        if (row >= a.H || xc.sums(row) != (pass == 0)) continue;
-        __nv_bfloat16 yv = __float2bfloat16_rn(0.f);
-        if (tp_ok) {
-          tp_ok = pass == 0 ? xc.reduce(t, row, yv) : xc.gather(t, row, yv);
-          if (!tp_ok) {
-            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-            yv = __float2bfloat16_rn(0.f);
-          }
-        }
-        y[(size_t)t * a.H + row] = yv;
-      }
-    }
+    const int nr = hi - lo;
+    tp_collect(xc, a.B * nr, [&](int i, int& t, int& row) {
+      t = i / nr;
+      row = j0 + lo + (i - t * nr);
+      return row < a.H;
+    }, reinterpret_cast<__nv_bfloat16*>(a.out), a.status);
   }
   if (tp && threadIdx.x == 0)
     for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += (int)gridDim.x) a.tp.epochs[c2] = tp_ep;

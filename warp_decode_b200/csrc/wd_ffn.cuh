@@ -454,9 +454,9 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   }
   if constexpr (kTP) {
     // This rank's partial rows go out first (TpCall: one-shot or two-shot);
-    // then the rows this rank sums, in rank order, and (two-shot) the rows
-    // whose owner sends the result.  A packet that does not arrive within
-    // 2 s gives a zero row and raises WD_STATUS_WAIT_TIMEOUT.
+    // then tp_collect: the rows this rank sums, in rank order, and (two-shot)
+    // the rows whose owner sends the result.  A packet that does not arrive
+    // within 2 s gives a zero row and raises WD_STATUS_WAIT_TIMEOUT.
     const TpCall xc{a.tp, tp_ep, a.H};
     for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
       const int b = i / nrows;
@@ -466,23 +466,11 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
       for (int w = 0; w < NCW; ++w) v += tiles[(size_t)w * tile + b * a.rows_max + lr];
       xc.push(b, r0 + lr, v);
     }
-    bool ok = true;
-    for (int pass = 0; pass < (a.tp.two_shot ? 2 : 1); ++pass) {
-      for (int i = threadIdx.x; i < a.B * nrows; i += blockDim.x) {
-        const int b = i / nrows;
-        const int row = r0 + (i - b * nrows);
-        if (xc.sums(row) != (pass == 0)) continue;
-        __nv_bfloat16 yv = __float2bfloat16_rn(0.f);
-        if (ok) {
-          ok = pass == 0 ? xc.reduce(b, row, yv) : xc.gather(b, row, yv);
-          if (!ok) {
-            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
-            yv = __float2bfloat16_rn(0.f);
-          }
-        }
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)b * H + row] = yv;
-      }
-    }
+    tp_collect(xc, a.B * nrows, [&](int i, int& b, int& row) {
+      b = i / nrows;
+      row = r0 + (i - b * nrows);
+      return true;
+    }, reinterpret_cast<__nv_bfloat16*>(a.out), a.status);
     if (threadIdx.x == 0)
       for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += G) a.tp.epochs[c2] = tp_ep;
   } else {

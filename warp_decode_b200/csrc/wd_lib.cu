@@ -1117,8 +1117,8 @@ struct TpComm {
 };
 
 // Bytes a rank sends one-shot (B x hidden x 8 x (world - 1)) above which the
-// automatic choice takes the two-shot exchange, which sends about
-// 2 / world of that at the price of a second NVLink latency.
+// automatic choice takes the two-shot exchange (from four ranks up), which
+// sends about 2 / world of that at the price of a second NVLink latency.
 // WARP_DECODE_TP_TWO_SHOT_BYTES overrides it.
 size_t tp_two_shot_bytes() {
   static const size_t v = [] {
@@ -1135,8 +1135,11 @@ wdb::TpArgs make_tp_args(const TpComm* c, int B) {
   tp.max_tokens = c->max_tokens;
   tp.max_ctas = c->max_ctas;
   tp.epochs = c->epochs;
+  // By size: two ranks send as many bytes two-shot as one-shot, so two-shot
+  // only from four ranks up.
   const size_t one_shot = (size_t)B * c->hidden * 8 * (c->world - 1);
-  tp.two_shot = c->exchange == 2 || (c->exchange == 0 && one_shot > tp_two_shot_bytes()) ? 1 : 0;
+  tp.two_shot = c->exchange == 2 ||
+                (c->exchange == 0 && c->world >= 4 && one_shot > tp_two_shot_bytes()) ? 1 : 0;
   for (int r = 0; r < c->world; ++r)
     tp.recv[r] = static_cast<unsigned long long*>(r == c->rank ? c->block : c->peer[r]);
   return tp;
