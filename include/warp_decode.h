@@ -177,19 +177,25 @@ WD_API int wd_set_down_path(int path);
  * Same arithmetic and tolerances as the two entry points.  For small calls
  * (automatic choice: B*topk <= 32; forced single launch: <= 64) with x, h of
  * the call fitting in shared memory (E <= 1024 when B*topk > 1) it is ONE
- * cooperative launch of one CTA per SM: the down weights stream while
- * gate_up still computes, and a grid barrier orders h.  Otherwise it runs the
- * two kernels of wd_moe_gate_up_3d_batched and wd_moe_down_3d_batched.  Requirements: hidden % 8 == 0, inter % 8 == 0, x,
+ * cooperative launch of one CTA per SM (SIMT): the down weights stream while
+ * gate_up still computes, and a grid barrier orders h.  For larger calls
+ * (automatic choice: B*topk >= 65, B <= 64, inter <= 2048) it is ONE
+ * cooperative launch on the tensor cores: the bodies of the two tcgen05
+ * kernels one after the other on the down kernel's clusters, the routing
+ * computed once, each CTA streaming its first down weights as soon as its
+ * gate_up items are done, and a grid barrier before h is read.  Otherwise it
+ * runs the two kernels of wd_moe_gate_up_3d_batched and
+ * wd_moe_down_3d_batched.  Requirements: hidden % 8 == 0, inter % 8 == 0, x,
  * the weights and h_buf 16-byte aligned.
  * sync: 8 bytes of device memory (8-byte aligned; a 64-bit grid-barrier
- * counter), zero before their first use; each single-launch call adds one per
- * CTA (the SM count) and needs nothing else reset.  The counter belongs to
+ * counter), zero before their first use; each single-launch call adds 4096 in
+ * total, whatever its grid, and needs nothing else reset.  The counter belongs to
  * one device.  NULL selects a counter owned by the library (one per device).
  * Calls that share a counter must not run at the same time (issue them on one
  * stream, or order them with events); give each concurrently used stream its
- * own.  Every CTA of a call adds its one arrival before it waits, also in a
- * call that ends in WD_STATUS_WAIT_TIMEOUT, so the counter stays a multiple
- * of the grid size and is never reset.
+ * own.  Every CTA of a call adds its share before it waits, also in a call
+ * that ends in WD_STATUS_WAIT_TIMEOUT, so between calls the counter stays a
+ * multiple of 4096 and is never reset.
  * Call once per device before capturing it in a CUDA graph (one-time device
  * setup).
  */
@@ -204,9 +210,11 @@ WD_API int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const voi
  * file-scope static device array of the library (256 B + 128 KiB per
  * device); calls with B*topk*inter*2 > 131072 bytes return
  * WD_ERR_UNSUPPORTED.  The array's counter starts zeroed at module load and,
- * as for wd_moe_ffn_3d_batched, stays a multiple of the grid size after every
- * call (a timed-out one included), so it needs no reset.  Every call on a device uses the same array, so calls that
- * overlap in time (other streams) race: serialise them.  The first call on a
+ * as for wd_moe_ffn_3d_batched, stays a multiple of 4096 after every call (a
+ * timed-out one included), so it needs no reset.  The kernels are those of
+ * wd_moe_ffn_3d_batched (same choice, same bits).  Every call on a device
+ * uses the same array, so calls that overlap in time (other streams) race:
+ * serialise them.  The first call on a
  * device looks up the array's address (cudaGetSymbolAddress) and must not be
  * made while that device's stream is being captured.
  */
@@ -232,9 +240,11 @@ WD_API int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk
 
 /*
  * Kernel choice behind wd_moe_ffn_3d_batched for later calls in this process:
- * 0 = automatic (single launch up to 32 routed slots), 1 = always the two
- * kernels, 2 = single launch wherever it applies (up to 64 routed slots).  WARP_DECODE_FFN=split|fused
- * sets the initial choice.
+ * 0 = automatic (SIMT single launch up to 32 routed slots, the two kernels up
+ * to 64, the tensor-core single launch above where it applies), 1 = always
+ * the two kernels, 2 = SIMT single launch wherever it applies (up to 64
+ * routed slots), 3 = tensor-core single launch wherever it applies (up to 64
+ * tokens).  WARP_DECODE_FFN=split|fused|tc sets the initial choice.
  */
 WD_API int wd_set_ffn_path(int path);
 

@@ -34,8 +34,8 @@ def test_gate_up_path_selector_validates():
     assert L.wd_set_down_path(-1) == capi.WD_ERR_SHAPE
     for p in (capi.PATH_SIMT, capi.PATH_TC, capi.PATH_AUTO):
         assert L.wd_set_down_path(p) == capi.WD_OK
-    assert L.wd_set_ffn_path(3) == capi.WD_ERR_SHAPE
-    for p in (capi.FFN_SPLIT, capi.FFN_FUSED, capi.FFN_AUTO):
+    assert L.wd_set_ffn_path(4) == capi.WD_ERR_SHAPE
+    for p in (capi.FFN_SPLIT, capi.FFN_FUSED, capi.FFN_TC, capi.FFN_AUTO):
         assert L.wd_set_ffn_path(p) == capi.WD_OK
 
 

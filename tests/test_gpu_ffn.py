@@ -2,8 +2,9 @@
 
 The entry point computes moe_down(moe_gate_up(x)) — the two calls the
 reference's callers make back to back (benchmark/bench.py:205,254-255 of
-Religious-J/warp_decode) — in one cooperative launch for up to 64 routed
-slots.  Checked through the C ABI: y within rtol = atol = 1e-2 of the
+Religious-J/warp_decode) — in one cooperative launch: the SIMT kernel for up
+to 64 routed slots, the tensor-core kernel (moe_ffn_tc_kernel, the bodies of
+the two tcgen05 kernels with one grid barrier between) up to 64 tokens.  Checked through the C ABI: y within rtol = atol = 1e-2 of the
 FP32-accumulated oracle, h bit-identical to the SIMT gate_up kernel, the split
 (two-kernel) path within the same tolerance, invalid expert ids, subgroups
 above the 8-member cap, FP32 output, caller-owned grid-barrier words, and
@@ -114,10 +115,18 @@ def test_qwen3_tp8(wd, B):
     finally:
         capi.set_ffn_path(capi.FFN_AUTO)
     assert np.array_equal(host_bits(y_t), host_bits(y))
-    # automatic choice: single launch up to 32 routed slots, two kernels above
+    # automatic choice: SIMT single launch up to 32 routed slots, the two
+    # kernels up to 64, the tensor-core single launch above
     y_auto, _, st = run_ffn(capi.FFN_AUTO, x, wgu, wdn, ids, scale)
     assert st == 0
-    assert np.array_equal(host_bits(y_auto), host_bits(y if B * c.topk <= 32 else y_split))
+    if B * c.topk <= 32:
+        assert np.array_equal(host_bits(y_auto), host_bits(y))
+    elif B * c.topk <= 64:
+        assert np.array_equal(host_bits(y_auto), host_bits(y_split))
+    else:
+        y_tc, _, st = run_ffn(capi.FFN_TC, x, wgu, wdn, ids, scale)
+        assert st == 0
+        assert np.array_equal(host_bits(y_auto), host_bits(y_tc))
 
 
 # (B, hidden, inter, E, topk, routing): ragged rows per CTA, small and large
@@ -168,10 +177,10 @@ def test_fp32_out_and_own_sync_words(wd):
     sync = torch.zeros(1, dtype=torch.int64, device="cuda")
     y32, _, st = run_ffn(capi.FFN_FUSED, x, wgu, wdn, ids, scale, sync=sync, out_fp32=True)
     assert st == 0
-    G = torch.cuda.get_device_properties(0).multi_processor_count
-    assert sync.item() == G, "barrier counter: one arrival per CTA (one CTA per SM)"
+    U = 4096  # GRID_BAR_UNITS: what one single-launch call adds, whatever its grid
+    assert sync.item() == U, "barrier counter: GRID_BAR_UNITS per launch"
     y16, _, st = run_ffn(capi.FFN_FUSED, x, wgu, wdn, ids, scale, sync=sync)
-    assert st == 0 and sync.item() == 2 * G
+    assert st == 0 and sync.item() == 2 * U
     assert np.array_equal(host_bits(y32.to(torch.bfloat16)), host_bits(y16))
     _, y_ref = oracle(x, wgu, wdn, ids, scale)
     check(host_bits(y16), y_ref, "fp32 output")
@@ -231,5 +240,108 @@ def test_launch_count(wd):
     g.replay()
     torch.cuda.synchronize()
     assert recorded == 1 and wd.launch_count() - n0 == 1
+    del g
+    assert wd.status(True, torch.cuda.current_device()) == 0
+
+
+# ---- tensor-core single launch (FFN_TC: moe_ffn_tc_kernel) ------------------
+@pytest.mark.parametrize("B", [1, 4, 8, 16, 33, 64])
+def test_tc_single_launch_qwen3(wd, B):
+    """y and h against the oracle, one launch per call, y within the
+    tolerance of the two-kernel path."""
+    c = W.CONFIGS["qwen3_235b_tp8"]
+    wgu, wdn = weights(c.hidden, c.inter, c.E, 41)
+    x, ids, scale = W.make_device_activations(B, c.hidden, c.E, c.topk, c.routing, 8800 + B)
+    n0 = wd.launch_count()
+    y, h, st = run_ffn(capi.FFN_TC, x, wgu, wdn, ids, scale)
+    assert st == 0
+    assert wd.launch_count() - n0 == 1, "one launch for the whole FFN"
+    h_ref, y_ref = oracle(x, wgu, wdn, ids, scale)
+    check(host_bits(h), h_ref, f"tc h B={B}")
+    check(host_bits(y), y_ref, f"tc y B={B}")
+    y_split, _, st = run_ffn(capi.FFN_SPLIT, x, wgu, wdn, ids, scale)
+    assert st == 0
+    check(host_bits(y), host_bits(y_split), f"tc vs split B={B}")
+
+
+# (B, hidden, inter, E, topk, routing): several down stages per item (inter
+# 768), 56 row tiles (hidden 7168), Zipf repeats with experts shared by more
+# than 16 slots (down items cut in runs of 16), top-1, ragged inter.
+TC_SHAPES = [
+    (3, 2048, 768, 64, 8, "uniform"),
+    (16, 2048, 768, 128, 8, "uniform"),
+    (4, 7168, 256, 256, 8, "zipf"),
+    (32, 7168, 256, 256, 8, "zipf"),
+    (48, 4096, 192, 16, 8, "uniform"),
+    (20, 4096, 192, 128, 1, "uniform"),
+    (9, 1024, 72, 32, 4, "uniform"),
+]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: "x".join(map(str, s[:5])) + s[5])
+def test_tc_single_launch_shapes(wd, shape):
+    B, H, I, E, K, law = shape
+    wgu, wdn = weights(H, I, E, 47)
+    x, ids, scale = W.make_device_activations(B, H, E, K, law, 8900 + B)
+    n0 = wd.launch_count()
+    y, h, st = run_ffn(capi.FFN_TC, x, wgu, wdn, ids, scale)
+    assert st == 0
+    assert wd.launch_count() - n0 == 1
+    h_ref, y_ref = oracle(x, wgu, wdn, ids, scale)
+    check(host_bits(h), h_ref, f"tc h {shape}")
+    check(host_bits(y), y_ref, f"tc y {shape}")
+
+
+def test_tc_single_launch_invalid_ids(wd):
+    B, H, I, E, K = 16, 4096, 192, 128, 8
+    wgu, wdn = weights(H, I, E, 41)
+    x, ids, scale = W.make_device_activations(B, H, E, K, "uniform", 9000)
+    ids[0, 1] = -1
+    ids[9, 7] = E + 5
+    y, h, st = run_ffn(capi.FFN_TC, x, wgu, wdn, ids, scale)
+    assert st & capi.WD_STATUS_BAD_EXPERT_ID
+    assert not st & capi.WD_STATUS_WAIT_TIMEOUT
+    h_ref, y_ref = oracle(x, wgu, wdn, ids, scale)
+    hb = host_bits(h)
+    assert np.all(hb[0 * K + 1] == 0) and np.all(hb[9 * K + 7] == 0)
+    check(hb, h_ref, "tc h next to invalid ids")
+    check(host_bits(y), y_ref, "tc y with invalid ids")
+
+
+def test_tc_and_simt_single_launch_share_the_barrier(wd):
+    """The two single-launch kernels (grids of different sizes) take turns on
+    one grid-barrier counter, caller-owned and library-owned, eagerly and in
+    a CUDA graph; every result stays the same."""
+    c = W.CONFIGS["qwen3_235b_tp8"]
+    wgu, wdn = weights(c.hidden, c.inter, c.E, 41)
+    xa, ia, sa = W.make_device_activations(2, c.hidden, c.E, c.topk, c.routing, 9100)
+    xb, ib, sb = W.make_device_activations(16, c.hidden, c.E, c.topk, c.routing, 9116)
+    sync = torch.zeros(1, dtype=torch.int64, device="cuda")
+    ya0, _, st = run_ffn(capi.FFN_FUSED, xa, wgu, wdn, ia, sa, sync=sync)
+    assert st == 0
+    yb0, _, st = run_ffn(capi.FFN_TC, xb, wgu, wdn, ib, sb, sync=sync)
+    assert st == 0
+    assert sync.item() == 2 * 4096
+    for s_ in (sync, None):
+        for _ in range(2):
+            ya, _, st = run_ffn(capi.FFN_FUSED, xa, wgu, wdn, ia, sa, sync=s_)
+            assert st == 0 and np.array_equal(host_bits(ya), host_bits(ya0))
+            yb, _, st = run_ffn(capi.FFN_TC, xb, wgu, wdn, ib, sb, sync=s_)
+            assert st == 0 and np.array_equal(host_bits(yb), host_bits(yb0))
+    capi.set_ffn_path(capi.FFN_AUTO)  # B=2: SIMT single launch, B=16: tensor-core
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        wd.moe_ffn_3d_batched(xa, wgu, wdn, ia, sa)
+        wd.moe_ffn_3d_batched(xb, wgu, wdn, ib, sb)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        ga = wd.moe_ffn_3d_batched(xa, wgu, wdn, ia, sa)
+        gb = wd.moe_ffn_3d_batched(xb, wgu, wdn, ib, sb)
+    for _ in range(4):
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(host_bits(ga), host_bits(ya0))
+        assert np.array_equal(host_bits(gb), host_bits(yb0))
     del g
     assert wd.status(True, torch.cuda.current_device()) == 0

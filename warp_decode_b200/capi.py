@@ -61,7 +61,7 @@ IPC_HANDLE_BYTES = 64
 GATE_UP_AUTO, GATE_UP_SIMT, GATE_UP_TC = 0, 1, 2
 PATH_AUTO, PATH_SIMT, PATH_TC = 0, 1, 2
 # Values of wd_set_ffn_path.
-FFN_AUTO, FFN_SPLIT, FFN_FUSED = 0, 1, 2
+FFN_AUTO, FFN_SPLIT, FFN_FUSED, FFN_TC = 0, 1, 2, 3
 
 _lib = None
 
@@ -137,7 +137,7 @@ def router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize, stre
 
 
 def set_ffn_path(path: int) -> None:
-    """Select the kernels behind wd_moe_ffn_3d_batched (FFN_AUTO / _SPLIT / _FUSED)."""
+    """Select the kernels behind wd_moe_ffn_3d_batched (FFN_AUTO / _SPLIT / _FUSED / _TC)."""
     check(lib().wd_set_ffn_path(int(path)))
 
 

@@ -267,6 +267,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "down kernel for later calls: 0 automatic, 1 SIMT, 2 tcgen05 tensor cores",
         py::arg("path"));
   m.def("set_ffn_path", &set_ffn_path,
-        "moe_ffn_3d_batched kernels for later calls: 0 automatic, 1 two launches, 2 one launch",
+        "moe_ffn_3d_batched kernels for later calls: 0 automatic, 1 two launches, 2 one SIMT "
+        "launch, 3 one tensor-core launch",
         py::arg("path"));
 }

@@ -545,6 +545,41 @@ __device__ inline void route_build(const RouteSmem& r, const int32_t* __restrict
   __syncthreads();
 }
 
+// Grid-scope counter accesses (grid barriers inside one launch) and L2 loads.
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add_u64(unsigned long long* p,
+                                                        unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// 16-byte load through L2 only (data written by other CTAs of this grid).
+__device__ __forceinline__ uint4 ldcg16(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+// Grid barriers of the single-launch kernels share one 64-bit counter (the
+// caller's `sync` words, or the library's): every launch adds exactly
+// GRID_BAR_UNITS in total, CTA c of G its share (c + 1) U / G - c U / G, so
+// between launches the counter is a multiple of U whatever grid each launch
+// used, and a CTA that reads the counter before adding its own share knows
+// the value that ends the barrier.  A CTA adds its share before it waits,
+// also on its abort paths, so the invariant survives a timed-out call.
+constexpr unsigned long long GRID_BAR_UNITS = 4096;  // >= every grid of the library
+__device__ __forceinline__ unsigned long long grid_bar_share() {
+  const unsigned long long c = blockIdx.x, G = gridDim.x;
+  return (c + 1) * GRID_BAR_UNITS / G - c * GRID_BAR_UNITS / G;
+}
+__device__ __forceinline__ unsigned long long grid_bar_target(unsigned long long at_entry) {
+  return (at_entry / GRID_BAR_UNITS + 1) * GRID_BAR_UNITS;
+}
+
 // System-scope release store / acquire load (flags shared with peer GPUs).
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

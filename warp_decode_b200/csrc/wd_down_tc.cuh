@@ -280,11 +280,16 @@ __host__ inline int down_tc_mx_smem_bytes(int stages, int sc, int nbuf, int conv
 // Body of both kernels.  kTP: the fused all-reduce variant (tp.world > 1);
 // the plain kernel carries none of its code.  kMx: MXFP8 weights.  kRoute:
 // routing code compiled for this launch's slot count (RouteMode).
-template <bool kTP, bool kMx, int kRoute>
-__device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const DownTcArgs a) {
+// kFused: phase 2 of moe_ffn_tc_kernel (FusedCtx: shared-memory region,
+// routing, top-k weights and TMEM given; h is written by the other CTAs of
+// the same launch, so the gather warps wait for the grid barrier and read h
+// through L2).  The weight stream starts before that wait.
+template <bool kTP, bool kMx, int kRoute, bool kFused = false>
+__device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const DownTcArgs a,
+                                             const FusedCtx* fx = nullptr) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  uint8_t* base = smem_raw + pad;
+  uint8_t* base = kFused ? fx->base : smem_raw + pad;
   const int S = a.stages, NB = a.nbuf, CL = a.cl;
   const int I = a.I;
   const int kc = down_tc_kc(I);
@@ -300,8 +305,8 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   uint8_t* conv = bring + (size_t)NB * BB;  // MXFP8: [CS] converted boxes
   uint8_t* sring = conv + (size_t)CS * TC_MX_CONV;  // MXFP8: [2] item scales
   float* Y = reinterpret_cast<float*>(sring + 2 * SCB);  // [B][128]
-  float* s_scale = Y + a.B * DTC_M;
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(s_scale + ((n * 4 + 127) / 128) * 32);
+  float* s_scale = kFused ? const_cast<float*>(fx->s_scale) : Y + a.B * DTC_M;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(Y + a.B * DTC_M + ((n * 4 + 127) / 128) * 32);
   uint64_t* wempty = wfull + S;
   uint64_t* bfull = wempty + S;
   uint64_t* bempty = bfull + NB;
@@ -315,7 +320,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + (kMx ? 2 : 0));
   volatile int* ctrl = reinterpret_cast<volatile int*>(tmem_slot + 4);
   int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
-  const RouteSmem r = route_carve(route_base, n, a.E, true);
+  const RouteSmem r = kFused ? *fx->r : route_carve(route_base, n, a.E, true);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rank = CL > 1 ? (int)cluster_ctarank() : 0;
@@ -350,18 +355,22 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
     fence_mbar_init();
   }
   if (threadIdx.x == 32) prefetch_tensormap(&tm_w);
-  if (warp == 1) {
+  if (!kFused && warp == 1) {
     tmem_alloc(tmem_slot, DTC_TMEM_COLS);
     tmem_relinquish();
     tc_fence_before();
   }
   for (int i = threadIdx.x; i < a.B * DTC_M; i += blockDim.x) Y[i] = 0.f;
-  // h, topk_scale (and possibly topk_ids) come from the preceding kernel.
-  pdl_wait_primary();
-  route_build<true, NoInit, kRoute>(r, a.ids, n, a.E, a.K, true, DTC_N, a.status, NoInit(), a.scale,
-                    s_scale);  // ends with __syncthreads
+  if constexpr (kFused) {
+    __syncthreads();
+  } else {
+    // h, topk_scale (and possibly topk_ids) come from the preceding kernel.
+    pdl_wait_primary();
+    route_build<true, NoInit, kRoute>(r, a.ids, n, a.E, a.K, true, DTC_N, a.status, NoInit(),
+                                      a.scale, s_scale);  // ends with __syncthreads
+  }
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = kFused ? fx->tmem : *tmem_slot;
   const int nsg = *r.nsg;
 
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -588,6 +597,23 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
     const int vecs = I / 8;  // 16-byte pieces per h row
     uint32_t its = 0;
     bool got = true;
+    if constexpr (kFused) {
+      // h of the whole launch: every CTA has added its arrivals after its
+      // gate_up phase (release); wait for all of them (acquire, bounded).
+      if (gw == 0 && lane == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu_u64(fx->sync) < fx->target) {
+          if (globaltimer_ns() - t0 > WD_WAIT_LIMIT_NS) {
+            raise_status(a.status, WD_STATUS_WAIT_TIMEOUT);
+            ctrl[0] = 1;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      named_barrier_sync(3, 32 * DTC_GW);
+    }
+    auto ldh = [&](const __nv_bfloat16* p) { return kFused ? ldcg16(p) : ldg16(p); };
     if (!kMx && nst == 1) {
       // one slice per item (inter <= 256): the item loop alone
       for (int g = g_first; g < nsg; g = next_item(g), ++its) {
@@ -602,7 +628,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
           const int c = rem >> 3, j = rem & 7;
           const int kv = c * 8 + j;
           uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (kv < vecs) v = ldg16(a.h + (size_t)r.members[beg + p] * I + kv * 8);
+          if (kv < vecs) v = ldh(a.h + (size_t)r.members[beg + p] * I + kv * 8);
           *reinterpret_cast<uint4*>(Bt + c * DTC_B_CHUNK + (p >> 3) * 1024 + (p & 7) * 128 +
                                     ((j ^ (p & 7)) << 4)) = v;
         }
@@ -625,7 +651,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
           const int c = rem >> 3, j = rem & 7;
           const int kv = (c0 + c) * 8 + j;
           uint4 v = make_uint4(0u, 0u, 0u, 0u);
-          if (kv < vecs) v = ldg16(a.h + (size_t)r.members[beg + p] * I + kv * 8);
+          if (kv < vecs) v = ldh(a.h + (size_t)r.members[beg + p] * I + kv * 8);
           *reinterpret_cast<uint4*>(Bt + c * DTC_B_CHUNK + (p >> 3) * 1024 + (p & 7) * 128 +
                                     ((j ^ (p & 7)) << 4)) = v;
         }
@@ -707,7 +733,7 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
   // tile (the 32 four-row units split as evenly as CL allows; CL need not
   // divide 128), 4 rows per thread.
   if (CL > 1) cluster_arrive();
-  if (warp == 1) {
+  if (!kFused && warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, DTC_TMEM_COLS);
   }

@@ -20,8 +20,8 @@
 //  * Phase 1 (gate_up) writes h to global memory (L2-resident, 3 KB/token).
 //  * Grid barrier (one thread per CTA, bounded wait): a 64-bit arrival
 //    counter in the caller's `sync` words that only ever grows (every launch
-//    adds exactly one arrival per CTA), so the target is known from the value
-//    read at kernel entry and arrival is a single release reduction.  Then
+//    adds exactly GRID_BAR_UNITS, grid_bar_share), so the target is known from
+//    the value read at kernel entry and arrival is a single release reduction.  Then
 //    every CTA copies the call's h into shared memory (over the x tile, no
 //    longer needed) with L2 loads.
 //  * Phase 2 (down): CTA c owns output rows [c*H/G, (c+1)*H/G) for every
@@ -81,24 +81,6 @@ __host__ inline int ffn_smem_bytes(int depth, int stage_bytes, int xh_bytes, int
          (NWARPS * depth + 1) * 8 + CTRL_INTS * 4 + route_smem_bytes(n, E, dedup);
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu_add_u64(unsigned long long* p,
-                                                        unsigned long long v) {
-  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-// 16-byte load through L2 only (data written by other CTAs of this grid).
-__device__ __forceinline__ uint4 ldcg16(const void* p) {
-  return __ldcg(reinterpret_cast<const uint4*>(p));
-}
 // Generic-proxy reads of a shared-memory slot before an async-proxy (bulk
 // copy) write into it.
 __device__ __forceinline__ void fence_proxy_async_shared() {
@@ -205,8 +187,8 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   const uint32_t tp_ep = kTP ? a.tp.epochs[blockIdx.x] + 1u : 0u;  // this call's epoch
 
   // Barrier counter at entry (used at the barrier): every earlier launch
-  // added exactly G arrivals and this CTA has not arrived yet, so
-  // floor(count / G) counts the earlier launches.
+  // added exactly GRID_BAR_UNITS and this CTA has not arrived yet, so
+  // floor(count / GRID_BAR_UNITS) counts the earlier launches.
   unsigned long long sync0 = 0ull;
   if (threadIdx.x == 0) {
     mbar_init(xbar, 1);
@@ -386,9 +368,8 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   // ---- grid barrier: every CTA's h rows written before any is read ----
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned long long bar_target =
-        (sync0 / (unsigned long long)G + 1ull) * (unsigned long long)G;
-    red_release_gpu_add_u64(a.sync, 1ull);
+    const unsigned long long bar_target = grid_bar_target(sync0);
+    red_release_gpu_add_u64(a.sync, grid_bar_share());
     const uint64_t t0 = globaltimer_ns();
     bool ok = true;
     while (ld_acquire_gpu_u64(a.sync) < bar_target) {

@@ -181,14 +181,18 @@ __device__ __forceinline__ void mx_convert_box(const uint8_t* src, uint8_t* dst,
 // Body of both kernels.  kMx: MXFP8 weights (tm_w over E4M3 bytes, tm_s over
 // the scales, converter warps); else bf16 weights.  kRoute: routing code
 // compiled for this launch's slot count (RouteMode).
-template <bool kMx, int kRoute>
+// kFused: phase 1 of moe_ffn_tc_kernel (FusedCtx: shared-memory region,
+// routing and TMEM given; the barriers are invalidated at the end so that the
+// down phase can reuse the memory).
+template <bool kMx, int kRoute, bool kFused = false>
 __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const CUtensorMap& tm_x,
-                                                const CUtensorMap* tm_s, const GateUpTcArgs a) {
-  pdl_launch_dependents();
+                                                const CUtensorMap* tm_s, const GateUpTcArgs a,
+                                                const FusedCtx* fx = nullptr) {
+  if constexpr (!kFused) pdl_launch_dependents();
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  uint8_t* base = smem_raw + pad;
+  uint8_t* base = kFused ? fx->base : smem_raw + pad;
   const int S = a.stages;
   const int KCH = a.kch;
   const int BT = a.npad * TC_BK * 2;  // bytes of one B chunk
@@ -219,7 +223,7 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
   int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
 
   const int n = a.B * a.K;
-  const RouteSmem r = route_carve(route_base, n, a.E, true);
+  const RouteSmem r = kFused ? *fx->r : route_carve(route_base, n, a.E, true);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -255,16 +259,21 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
       prefetch_tensormap(&tm_x);
       if (kMx) prefetch_tensormap(tm_s);
     }
-    if (warp == 1) {
+    if (!kFused && warp == 1) {
       tmem_alloc(tmem_slot, TC_TMEM_COLS);
       tmem_relinquish();
       tc_fence_before();
     }
   };
-  route_build<false, decltype(setup), kRoute>(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status,
-                                             setup);  // ends with __syncthreads
+  if constexpr (kFused) {
+    setup();
+    __syncthreads();
+  } else {
+    route_build<false, decltype(setup), kRoute>(r, a.ids, n, a.E, a.K, true, MAX_SLOTS, a.status,
+                                               setup);  // ends with __syncthreads
+  }
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = kFused ? fx->tmem : *tmem_slot;
 
   const int n_tiles = (a.I + TC_NEUR - 1) / TC_NEUR;
   const int items = *r.nsg * n_tiles;
@@ -576,12 +585,22 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (!kFused && warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);
   }
   // No CTA leaves while a peer may still write into its shared memory.
   if (CL > 1) cluster_sync();
+  if constexpr (kFused) {
+    // Every wait and every arrive (local or from the cluster) is done.  This
+    // thread's generic shared-memory writes (the epilogue's exchange) are
+    // ordered before the down phase's bulk copies into the same bytes.
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < 2 * S + 9 + 2 * CS + 2 * SX; ++i) mbar_inval(full + i);
+    }
+    __syncthreads();
+  }
 }
 
 template <int kRoute>

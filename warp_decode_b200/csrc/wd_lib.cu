@@ -26,12 +26,13 @@
 #include "wd_gate_up_tc.cuh"
 #include "wd_down_tc.cuh"
 #include "wd_ffn.cuh"
+#include "wd_ffn_tc.cuh"
 #include "wd_router.cuh"
 
 // Scratch of wd_moe_ffn_3d_batched_noalloc: [0, 8) the grid-barrier counter
-// (zero at module load; each single-launch call adds one per CTA, so it never
-// needs resetting), [256, 256 + 128 KiB) h of the call (B*topk*inter bf16, at
-// most 64 routed slots x 1024 inter).  One copy per device; calls that overlap
+// (zero at module load; each single-launch call adds GRID_BAR_UNITS in total,
+// so it never needs resetting), [256, 256 + 128 KiB) h of the call
+// (B*topk*inter bf16, e.g. 64 routed slots x 1024 inter).  One copy per device; calls that overlap
 // in time race on it.
 constexpr size_t kNoallocHeader = 256;
 constexpr size_t kNoallocHBytes = (size_t)64 * 1024 * 2;
@@ -60,6 +61,7 @@ struct DeviceInfo {
   int smem_reserved = 0;    // shared memory the runtime reserves per CTA
   unsigned long long* ffn_sync = nullptr;  // library-owned grid-barrier counter (g_wd_ffn_sync)
   unsigned char* noalloc_scratch = nullptr;  // g_wd_noalloc_scratch, set on first use
+  std::atomic<bool> ffn_tc_off{false};  // moe_ffn_tc_kernel's launch was refused once
   bool ready = false;
 };
 
@@ -103,6 +105,8 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_down_tc_mx_kernel<wdb::ROUTE_LARGE>),
         reinterpret_cast<const void*>(&wdb::moe_ffn_kernel<false>),
         reinterpret_cast<const void*>(&wdb::moe_ffn_kernel<true>),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_tc_kernel<wdb::ROUTE_SMALL>),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_tc_kernel<wdb::ROUTE_LARGE>),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -193,10 +197,12 @@ int kernel_path(std::atomic<int>& slot, const char* env) {
 int gate_up_path() { return kernel_path(g_gate_up_path, "WARP_DECODE_GATE_UP"); }
 int down_path() { return kernel_path(g_down_path, "WARP_DECODE_DOWN"); }
 
-// FFN entry point: 0 = automatic (single launch up to WD_FFN_AUTO_MAX_SLOTS
-// routed slots), 1 = always the two kernels, 2 = single launch wherever it
-// applies (up to 64 routed slots).
-// WARP_DECODE_FFN=split|fused sets the initial choice.
+// FFN entry point: 0 = automatic (SIMT single launch up to
+// WD_FFN_AUTO_MAX_SLOTS routed slots, the tensor-core single launch above
+// where it applies), 1 = always the two kernels, 2 = SIMT single launch
+// wherever it applies (up to 64 routed slots), 3 = tensor-core single launch
+// wherever it applies.
+// WARP_DECODE_FFN=split|fused|tc sets the initial choice.
 std::atomic<int> g_ffn_path{-1};
 int ffn_path() {
   int p = g_ffn_path.load(std::memory_order_relaxed);
@@ -205,6 +211,7 @@ int ffn_path() {
     p = 0;
     if (v && std::strcmp(v, "split") == 0) p = 1;
     if (v && std::strcmp(v, "fused") == 0) p = 2;
+    if (v && std::strcmp(v, "tc") == 0) p = 3;
     int expected = -1;
     g_ffn_path.compare_exchange_strong(expected, p);
     p = g_ffn_path.load(std::memory_order_relaxed);
@@ -1017,6 +1024,15 @@ bool ffn_fits(const DeviceInfo* dev, int smem) {
 #define WD_FFN_AUTO_MAX_SLOTS 32
 #endif
 
+// Routed slots from which the automatic choice takes the tensor-core single
+// launch (moe_ffn_tc_kernel) where it applies.  Measured on B200 (H 4096,
+// I 192, E 128, top-8, cold L2, us): B = 8 63.0 vs 61.8 as SIMT gate_up +
+// tensor-core down; B = 16 86.2 vs 91.8; B = 32 114.6 / 111.9 vs 112.7 (two
+// runs); B = 64 123.4 vs 129.1 as the two tensor-core kernels.
+#ifndef WD_FFN_TC_MIN_SLOTS
+#define WD_FFN_TC_MIN_SLOTS 65
+#endif
+
 // Launch geometry of the single-launch FFN, or false where it does not apply:
 // more than max_slots routed slots (at most 64), E above the dedup table, or
 // x / h of the call too large for shared memory next to a two-slot ring.
@@ -1101,6 +1117,220 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
                        : cudaLaunchKernelEx(&cfg, wdb::moe_ffn_kernel<false>, a);
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("ffn launch: ") + cudaGetErrorString(err));
+  note_launch();
+  return WD_OK;
+}
+
+// ---- single-launch FFN on the tensor cores ----------------------------------
+struct FfnTcPlan {
+  int smem = 0, cl = 0, tiles = 0, npad = 0, route_bytes = 0;
+  int gu_stages = 0, kch = 0, gu_cl = 1;
+  int dn_stages = 0, dn_sc = 0, dn_nb = 0;
+};
+
+// Largest cluster size cl <= 8 such that the tiles x cl CTAs of
+// moe_ffn_tc_kernel with `smem` bytes are all resident at once (the grid
+// barrier needs them co-resident); 0 if none.  Cached per device and smem.
+int ffn_tc_cluster(const DeviceInfo* dev, int tiles, int smem) {
+  static std::mutex mu;
+  static std::vector<std::array<int, 4>> cache;  // {device, tiles, smem, cl}
+  int devno = 0;
+  cudaGetDevice(&devno);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& c : cache)
+      if (c[0] == devno && c[1] == tiles && c[2] == smem) return c[3];
+  }
+  int best = 0;
+  for (int cl = 8; cl >= 2 && !best; --cl) {
+    if (tiles * cl > dev->sm_count) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(tiles * cl));
+    cfg.blockDim = dim3(wdb::DTC_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, wdb::moe_ffn_tc_kernel<wdb::ROUTE_LARGE>, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (nc >= tiles) best = cl;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({devno, tiles, smem, best});
+  return best;
+}
+
+// Launch geometry of moe_ffn_tc_kernel, or false where it does not apply:
+// one launch of at most TC_NMAX tokens and MAX_SLOTS routed slots, the
+// shapes of both tensor-core kernels, both phases' rings next to the routing
+// region in shared memory, and every CTA resident at once.
+bool ffn_tc_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int inter,
+                 FfnTcPlan* out) {
+  const int n = B * topk;
+  if (B < 1 || B > wdb::TC_NMAX || n > wdb::MAX_SLOTS) return false;
+  if (E > wdb::MAX_DEDUP_E || hidden % 8 != 0 || inter % 8 != 0) return false;
+  if (inter > wdb::DTC_MAXKC * wdb::DTC_BK) return false;
+  FfnTcPlan p;
+  p.tiles = (hidden + wdb::DTC_M - 1) / wdb::DTC_M;
+  p.npad = (B + 15) / 16 * 16;
+  p.kch = WD_TC_KCH;
+  p.route_bytes = wdb::ffn_tc_route_bytes(n, E);
+  const int route = wdb::route_smem_bytes(n, E, true);
+  const int budget = dev->smem_optin - 2048 - p.route_bytes;
+  auto gu_plan = [&](int cl, int* stages) {
+    for (int st = 8; st >= 2; --st) {
+      const int need = wdb::gate_up_tc_smem_bytes(st, p.kch, p.npad, n, E, cl) - route;
+      if (need <= budget) { *stages = st; return need; }
+    }
+    return 0;
+  };
+  int gu = gu_plan(1, &p.gu_stages);
+  if (!gu) return false;
+  const int kc = wdb::down_tc_kc(inter);
+  int dn = 0;
+  for (int c : {wdb::DTC_SC, 2, 1}) {
+    const int scc = std::min(c, kc);
+    for (int st = 6; st >= 2 && !dn; --st)
+      for (int nb : {8, 6, wdb::DTC_GW}) {
+        const int need = wdb::down_tc_smem_bytes(st, scc, nb, inter, B, n, E) - route;
+        if (need <= budget) {
+          dn = need; p.dn_stages = st; p.dn_sc = scc; p.dn_nb = nb;
+          break;
+        }
+      }
+    if (dn) break;
+  }
+  if (!dn) return false;
+  p.smem = 1024 + p.route_bytes + std::max(gu, dn);
+  if (p.smem > dev->smem_optin - 1024) return false;
+  p.cl = ffn_tc_cluster(dev, p.tiles, p.smem);
+  if (p.cl == 0) return false;
+  // The gate_up phase splits K over the launch's clusters when that lowers
+  // the busiest CTA's share: whole items on tiles x cl CTAs, against
+  // ceil(items / clusters) / cl (items estimated from the expected distinct
+  // experts under uniform routing).  Measured (H 4096, I 192, E 128, top-8):
+  // at B = 8 (about 150 items on 128 CTAs) whole items left most CTAs idle
+  // while a quarter streamed a second item.
+  const int n_tiles = (inter + wdb::TC_NEUR - 1) / wdb::TC_NEUR;
+  const double u_est = E * (1.0 - std::pow(1.0 - std::min(topk, E) / (double)E, (double)B));
+  const int items = std::max(1, (int)std::ceil(u_est)) * n_tiles;
+  const int ctas = p.tiles * p.cl;
+  const double cost1 = std::ceil((double)items / ctas);
+  const double costc = std::ceil((double)items / p.tiles) / p.cl + 0.02 * (p.cl - 1);
+  int st_c = 0;
+  const int gu_c = costc < cost1 ? gu_plan(p.cl, &st_c) : 0;
+  if (gu_c) {
+    const int smem_c = 1024 + p.route_bytes + std::max(gu_c, dn);
+    if (smem_c <= dev->smem_optin - 1024 && ffn_tc_cluster(dev, p.tiles, smem_c) == p.cl) {
+      p.gu_cl = p.cl;
+      p.gu_stages = st_c;
+      p.smem = smem_c;
+    }
+  }
+  *out = p;
+  return true;
+}
+
+// One cooperative launch of moe_ffn_tc_kernel (clusters of p.cl).  Returns
+// WD_ERR_UNSUPPORTED, with nothing launched, if the runtime refuses the
+// cooperative cluster launch, so the caller can take the two kernels.
+int ffn_tc_launch(const DeviceInfo* dev, const FfnTcPlan& p, const void* x, const void* w_gu,
+                  const void* w_dn, const int32_t* ids, const float* scale, void* h,
+                  unsigned long long* sync, void* y, int out_fp32, int B, int E, int topk,
+                  int hidden, int inter, uint32_t* status, cudaStream_t s) {
+  (void)dev;
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t ones[4] = {1, 1, 1, 1};
+  // gate_up weights as (k, neuron, gate|up, expert), boxes of 64 K x 64 gate
+  // + 64 up rows; x boxes of 64 K x npad tokens (as gate_up_tc_launch).
+  CUtensorMap tm_gw, tm_x, tm_dw;
+  const cuuint64_t wdim[4] = {(cuuint64_t)hidden, (cuuint64_t)inter, 2, (cuuint64_t)E};
+  const cuuint64_t wstr[3] = {(cuuint64_t)hidden * 2, (cuuint64_t)inter * hidden * 2,
+                              (cuuint64_t)2 * inter * hidden * 2};
+  const cuuint32_t wbox[4] = {(cuuint32_t)wdb::TC_BK, (cuuint32_t)wdb::TC_NEUR, 2, 1};
+  CUresult cr = enc(&tm_gw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(w_gu), wdim,
+                    wstr, wbox, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    WD_TC_L2PROMO, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_gate_up) encode failed");
+  const cuuint64_t xdim[2] = {(cuuint64_t)hidden, (cuuint64_t)B};
+  const cuuint64_t xstr[1] = {(cuuint64_t)hidden * 2};
+  const cuuint32_t xbox[2] = {(cuuint32_t)wdb::TC_BK, (cuuint32_t)p.npad};
+  cr = enc(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdim, xstr, xbox,
+           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (x) encode failed");
+  // down weights [E, H, I]: boxes of 64 K x 128 rows of one expert.
+  const cuuint64_t ddim[3] = {(cuuint64_t)inter, (cuuint64_t)hidden, (cuuint64_t)E};
+  const cuuint64_t dstr[2] = {(cuuint64_t)inter * 2, (cuuint64_t)hidden * inter * 2};
+  const cuuint32_t dbox[3] = {(cuuint32_t)wdb::DTC_BK, (cuuint32_t)wdb::DTC_M, 1};
+  cr = enc(&tm_dw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w_dn), ddim, dstr, dbox,
+           ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(WD_ERR_CUDA, "tensor map (w_down) encode failed");
+
+  wdb::FfnTcArgs a = {};
+  a.gu.ids = ids;
+  a.gu.out = reinterpret_cast<__nv_bfloat16*>(h);
+  a.gu.status = status;
+  a.gu.B = B; a.gu.E = E; a.gu.K = topk; a.gu.H = hidden; a.gu.I = inter;
+  a.gu.stages = p.gu_stages;
+  a.gu.npad = p.npad;
+  a.gu.kch = p.kch;
+  a.gu.cl = p.gu_cl;
+  a.gu.conv = 0;
+  a.gu.xstages = 0;
+  a.dn.h = reinterpret_cast<const __nv_bfloat16*>(h);
+  a.dn.ids = ids;
+  a.dn.scale = scale;
+  a.dn.out = y;
+  a.dn.out_fp32 = out_fp32 ? 1 : 0;
+  a.dn.status = status;
+  a.dn.B = B; a.dn.E = E; a.dn.K = topk; a.dn.H = hidden; a.dn.I = inter;
+  a.dn.stages = p.dn_stages;
+  a.dn.sc = p.dn_sc;
+  a.dn.nbuf = p.dn_nb;
+  a.dn.cl = p.cl;
+  a.dn.tp = {};
+  a.dn.wscale = nullptr;
+  a.dn.conv = 0;
+  a.ids = ids;
+  a.scale = scale;
+  a.sync = sync;
+  a.B = B; a.E = E; a.K = topk;
+  a.route_bytes = p.route_bytes;
+
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.tiles * p.cl));
+  cfg.blockDim = dim3(wdb::DTC_THREADS);
+  cfg.dynamicSmemBytes = (size_t)p.smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err =
+      B * topk <= 64
+          ? cudaLaunchKernelEx(&cfg, wdb::moe_ffn_tc_kernel<wdb::ROUTE_SMALL>, tm_gw, tm_x, tm_dw, a)
+          : cudaLaunchKernelEx(&cfg, wdb::moe_ffn_tc_kernel<wdb::ROUTE_LARGE>, tm_gw, tm_x, tm_dw, a);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return fail(WD_ERR_UNSUPPORTED, std::string("ffn (tensor core) launch: ") +
+                                        cudaGetErrorString(err));
+  }
   note_launch();
   return WD_OK;
 }
@@ -1248,8 +1478,8 @@ int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
 
 int wd_set_ffn_path(int path) {
   g_last_error.clear();
-  if (path < 0 || path > 2)
-    return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (split) or 2 (fused)");
+  if (path < 0 || path > 3)
+    return fail(WD_ERR_SHAPE, "path must be 0 (auto), 1 (split), 2 (fused) or 3 (tensor-core fused)");
   g_ffn_path.store(path);
   return WD_OK;
 }
@@ -1274,12 +1504,23 @@ int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_do
   if ((rc = device_info(&dev))) return rc;
   FfnPlan plan;
   const int fp = ffn_path();
-  if (fp != 1 && ffn_plan(dev, B, E, topk, hidden, inter,
-                          fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
-    return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
-                      sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, out_fp32, B,
-                      E, topk, hidden, inter,
+  uint32_t* const bar = sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync);
+  if ((fp == 0 || fp == 2) &&
+      ffn_plan(dev, B, E, topk, hidden, inter,
+               fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
+    return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf, bar, y_out,
+                      out_fp32, B, E, topk, hidden, inter,
                       status, reinterpret_cast<cudaStream_t>(stream));
+  FfnTcPlan tplan;
+  if ((fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) && !dev->ffn_tc_off &&
+      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan)) {
+    rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
+                       reinterpret_cast<unsigned long long*>(bar), y_out, out_fp32, B, E, topk,
+                       hidden, inter, status, reinterpret_cast<cudaStream_t>(stream));
+    if (rc != WD_ERR_UNSUPPORTED) return rc;
+    dev->ffn_tc_off = true;  // the runtime refused the cooperative cluster launch: not again
+    g_last_error.clear();
+  }
   rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
                                  topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
   if (rc) return rc;
@@ -1319,11 +1560,22 @@ int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, const vo
   void* h_buf = dev->noalloc_scratch + kNoallocHeader;
   FfnPlan plan;
   const int fp = ffn_path();
-  if (fp != 1 && ffn_plan(dev, B, E, topk, hidden, inter,
-                          fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
+  if ((fp == 0 || fp == 2) &&
+      ffn_plan(dev, B, E, topk, hidden, inter,
+               fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
     return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf, sync, y_out,
                       out_fp32, B, E, topk, hidden, inter, status,
                       reinterpret_cast<cudaStream_t>(stream));
+  FfnTcPlan tplan;
+  if ((fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) && !dev->ffn_tc_off &&
+      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan)) {
+    rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
+                       reinterpret_cast<unsigned long long*>(sync), y_out, out_fp32, B, E, topk,
+                       hidden, inter, status, reinterpret_cast<cudaStream_t>(stream));
+    if (rc != WD_ERR_UNSUPPORTED) return rc;
+    dev->ffn_tc_off = true;
+    g_last_error.clear();
+  }
   rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
                                  topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
   if (rc) return rc;

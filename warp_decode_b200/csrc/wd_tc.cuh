@@ -228,6 +228,26 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&v)[16]) {
       : "memory");
 }
 
+// Invalidate an mbarrier whose shared memory is about to be reused.
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// What the single-launch tensor-core FFN (moe_ffn_tc_kernel) hands to the
+// gate_up and down bodies it runs one after the other: the shared-memory
+// region a phase may carve, the call's routing (computed once), the
+// top-k weights in shared memory, the TMEM columns (allocated once), and,
+// for the down phase, the grid barrier its h gather waits for.
+struct RouteSmem;
+struct FusedCtx {
+  uint8_t* base;                // 1024-aligned phase region
+  const RouteSmem* r;           // routing for this phase
+  const float* s_scale;         // topk_scale of the call (down phase)
+  uint32_t tmem;                // TMEM base address
+  unsigned long long* sync;     // grid-barrier counter
+  unsigned long long target;    // value that releases the down phase's h gather
+};
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
