@@ -292,10 +292,11 @@ WD_API int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down,
 /*
  * The whole tensor-parallel FFN with the all-reduce fused in (no counterpart
  * in the reference): this rank's gate_up / down shards, then y_out = bf16
- * sum over all ranks (identical bits on every rank).  Where the single
- * launch of wd_moe_ffn_3d_batched applies (B*topk <= 32 automatically, and
- * B <= the communicator's max_tokens) that one cooperative kernel also does
- * the exchange; otherwise gate_up, then wd_moe_down_3d_batched_allreduce.
+ * sum over all ranks (identical bits on every rank).  Where one of the single
+ * launches of wd_moe_ffn_3d_batched applies (SIMT: B*topk <= 32
+ * automatically; tensor cores: B*topk >= 65; both with B <= the
+ * communicator's max_tokens) that one cooperative kernel also does the
+ * exchange; otherwise gate_up, then wd_moe_down_3d_batched_allreduce.
  * h_buf / sync as for wd_moe_ffn_3d_batched; collective rules as above.
  */
 WD_API int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up,

@@ -108,6 +108,17 @@ __device__ __forceinline__ unsigned long long tp_peek(const unsigned long long* 
   asm volatile("ld.volatile.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
+// Four packets of consecutive rows in one 32-byte vector store (p 32-byte
+// aligned): each 64-bit element is still one single-copy-atomic packet, and
+// a warp's stores cover whole sectors instead of a quarter of each.
+__device__ __forceinline__ void tp_put4(unsigned long long* p, const float (&v)[4], uint32_t ep) {
+  const unsigned long long e = (unsigned long long)ep << 32;
+  asm volatile("st.volatile.global.v4.b64 [%0], {%1, %2, %3, %4};" ::"l"(p),
+               "l"(e | __float_as_uint(v[0])), "l"(e | __float_as_uint(v[1])),
+               "l"(e | __float_as_uint(v[2])), "l"(e | __float_as_uint(v[3]))
+               : "memory");
+}
+
 // The value of the packet at p once it carries epoch ep; false if it did not
 // arrive within WD_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool tp_take(const unsigned long long* p, uint32_t ep, float& v) {
@@ -145,6 +156,16 @@ struct TpCall {
       for (int r = 0; r < tp.world; ++r) tp_put(at(r, tp.rank, t, row), v, ep);
     }
   }
+  // This rank's partials of rows row..row + 3 of token t (row % 4 == 0, all
+  // four below H; H % 4 == 0, so the packets are 32-byte aligned): one
+  // vector store per destination rank.
+  __device__ void push4(int t, int row, const float (&v)[4]) const {
+    if (tp.two_shot) {
+      tp_put4(at(owner(row), tp.rank, t, row), v, ep);
+    } else {
+      for (int r = 0; r < tp.world; ++r) tp_put4(at(r, tp.rank, t, row), v, ep);
+    }
+  }
   // The value of the packet at p, given a first reading w, once it carries
   // this call's epoch; false if it did not arrive within WD_WAIT_LIMIT_NS.
   __device__ bool settle(const unsigned long long* p, unsigned long long w, float& v) const {
@@ -161,11 +182,17 @@ struct TpCall {
   // Sum of every rank's partial of (t, row) in rank order (a row this rank
   // sums; the ranks' packets are read together, then any late one polled);
   // two-shot also sends the bf16 result to the other ranks.
-  __device__ bool reduce(int t, int row, __nv_bfloat16& y) const {
-    unsigned long long w[TP_MAX_WORLD];
+  // The ranks' packets of (t, row) in this rank's buffer, read together.
+  __device__ void peek_all(int t, int row, unsigned long long (&w)[TP_MAX_WORLD]) const {
 #pragma unroll
     for (int r = 0; r < TP_MAX_WORLD; ++r)
       if (r < tp.world) w[r] = tp_peek(at(tp.rank, r, t, row));
+  }
+  // Sum of every rank's partial of (t, row) in rank order, from first
+  // readings w (a row this rank sums; any late packet is polled); two-shot
+  // also sends the bf16 result to the other ranks.
+  __device__ bool reduce(int t, int row, const unsigned long long (&w)[TP_MAX_WORLD],
+                         __nv_bfloat16& y) const {
     float s = 0.f;
 #pragma unroll
     for (int r = 0; r < TP_MAX_WORLD; ++r) {
@@ -188,24 +215,37 @@ struct TpCall {
 // This rank's output rows of the call after its pushes: entry i (i =
 // threadIdx.x, + blockDim.x, ... < n) is (t, row) = entry(i), skipped where
 // entry() returns false.  First the rows this rank sums (all one-shot), then
-// (two-shot) the other rows from their owners, eight entries per thread in
-// flight.  A packet that does not arrive within the bound gives a zero and
-// raises WD_STATUS_WAIT_TIMEOUT; returns false then.
+// (two-shot) the other rows from their owners; the packets of four (sums)
+// or eight (owners' results) entries per thread are in flight together.  A
+// packet that does not arrive within the bound gives a zero and raises
+// WD_STATUS_WAIT_TIMEOUT; returns false then.
 template <class Entry>
 __device__ inline bool tp_collect(const TpCall& xc, int n, Entry entry, __nv_bfloat16* y,
                                   uint32_t* status) {
   bool ok = true;
   const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    int t, row;
-    if (!entry(i, t, row) || !xc.sums(row)) continue;
-    __nv_bfloat16 yv = zero;
-    if (ok && !xc.reduce(t, row, yv)) {
-      ok = false;
-      yv = zero;
-      raise_status(status, WD_STATUS_WAIT_TIMEOUT);
+  constexpr int RB = 4;  // entries per thread whose packets are in flight together
+  for (int i0 = threadIdx.x; i0 < n; i0 += RB * (int)blockDim.x) {
+    int tt[RB], rr[RB];
+    bool take[RB];
+    unsigned long long w[RB][TP_MAX_WORLD];
+#pragma unroll
+    for (int j = 0; j < RB; ++j) {
+      const int i = i0 + j * (int)blockDim.x;
+      take[j] = i < n && entry(i, tt[j], rr[j]) && xc.sums(rr[j]);
+      if (take[j]) xc.peek_all(tt[j], rr[j], w[j]);
     }
-    y[(size_t)t * xc.H + row] = yv;
+#pragma unroll
+    for (int j = 0; j < RB; ++j) {
+      if (!take[j]) continue;
+      __nv_bfloat16 yv = zero;
+      if (ok && !xc.reduce(tt[j], rr[j], w[j], yv)) {
+        ok = false;
+        yv = zero;
+        raise_status(status, WD_STATUS_WAIT_TIMEOUT);
+      }
+      y[(size_t)tt[j] * xc.H + rr[j]] = yv;
+    }
   }
   if (!xc.tp.two_shot) return ok;
   constexpr int GB = 8;
@@ -765,9 +805,13 @@ __device__ __forceinline__ void down_tc_body(const CUtensorMap& tm_w, const Down
     const float v[4] = {acc.x, acc.y, acc.z, acc.w};
     if constexpr (kTP) if (tp) {
       // This rank's partials of the rows go out first (no wait in between).
+      if (j0 + jj + 3 < a.H && (a.H & 3) == 0) {
+        xc.push4(t, j0 + jj, v);
+      } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (j0 + jj + u < a.H) xc.push(t, j0 + jj + u, v[u]);
+        for (int u = 0; u < 4; ++u)
+          if (j0 + jj + u < a.H) xc.push(t, j0 + jj + u, v[u]);
+      }
       continue;
     }
 #pragma unroll

@@ -50,7 +50,9 @@ __host__ __device__ inline int ffn_tc_route_bytes(int n, int E) {
   return (b + 1023) / 1024 * 1024;
 }
 
-template <int kRoute>
+// kTP: the down phase ends in the fused all-reduce of the tensor-core down
+// kernel (fa.dn.tp: y = bf16 sum over the group's ranks).
+template <int kRoute, bool kTP = false>
 __global__ void __launch_bounds__(DTC_THREADS, 1)
     moe_ffn_tc_kernel(const __grid_constant__ CUtensorMap tm_gw,
                       const __grid_constant__ CUtensorMap tm_x,
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
   rd.nsg = dsg + 3 * n;
   fx.r = &rd;
   fx.target = grid_bar_target(sync0);
-  down_tc_body<false, false, kRoute, true>(tm_dw, fa.dn, &fx);
+  down_tc_body<kTP, false, kRoute, true>(tm_dw, fa.dn, &fx);
 
   tc_fence_before();
   __syncthreads();

@@ -107,6 +107,7 @@ int device_info(DeviceInfo** out) {
         reinterpret_cast<const void*>(&wdb::moe_ffn_kernel<true>),
         reinterpret_cast<const void*>(&wdb::moe_ffn_tc_kernel<wdb::ROUTE_SMALL>),
         reinterpret_cast<const void*>(&wdb::moe_ffn_tc_kernel<wdb::ROUTE_LARGE>),
+        reinterpret_cast<const void*>(&wdb::moe_ffn_tc_kernel<wdb::ROUTE_ANY, true>),
     };
     for (const void* k : kernels) {
       if (err != cudaSuccess) break;
@@ -1245,7 +1246,8 @@ bool ffn_tc_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int 
 int ffn_tc_launch(const DeviceInfo* dev, const FfnTcPlan& p, const void* x, const void* w_gu,
                   const void* w_dn, const int32_t* ids, const float* scale, void* h,
                   unsigned long long* sync, void* y, int out_fp32, int B, int E, int topk,
-                  int hidden, int inter, uint32_t* status, cudaStream_t s) {
+                  int hidden, int inter, uint32_t* status, cudaStream_t s,
+                  const wdb::TpArgs* tp = nullptr) {
   (void)dev;
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return fail(WD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1300,6 +1302,11 @@ int ffn_tc_launch(const DeviceInfo* dev, const FfnTcPlan& p, const void* x, cons
   a.dn.nbuf = p.dn_nb;
   a.dn.cl = p.cl;
   a.dn.tp = {};
+  if (tp) {
+    if (p.tiles * p.cl > tp->max_ctas)
+      return fail(WD_ERR_UNSUPPORTED, "grid larger than the communicator's epoch array");
+    a.dn.tp = *tp;
+  }
   a.dn.wscale = nullptr;
   a.dn.conv = 0;
   a.ids = ids;
@@ -1323,7 +1330,9 @@ int ffn_tc_launch(const DeviceInfo* dev, const FfnTcPlan& p, const void* x, cons
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const cudaError_t err =
-      B * topk <= 64
+      tp          ? cudaLaunchKernelEx(&cfg, wdb::moe_ffn_tc_kernel<wdb::ROUTE_ANY, true>, tm_gw,
+                                       tm_x, tm_dw, a)
+      : B * topk <= 64
           ? cudaLaunchKernelEx(&cfg, wdb::moe_ffn_tc_kernel<wdb::ROUTE_SMALL>, tm_gw, tm_x, tm_dw, a)
           : cudaLaunchKernelEx(&cfg, wdb::moe_ffn_tc_kernel<wdb::ROUTE_LARGE>, tm_gw, tm_x, tm_dw, a);
   if (err != cudaSuccess) {
@@ -1719,7 +1728,7 @@ int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up, const 
   if ((rc = device_info(&dev))) return rc;
   FfnPlan plan;
   const int fp = ffn_path();
-  if (fp != 1 && B <= c->max_tokens &&
+  if ((fp == 0 || fp == 2) && B <= c->max_tokens &&
       ffn_plan(dev, B, E, topk, hidden, inter,
                fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan) &&
       plan.grid <= c->max_ctas) {
@@ -1727,6 +1736,20 @@ int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up, const 
     return ffn_launch(dev, plan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
                       sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync), y_out, 0, B, E,
                       topk, hidden, inter, status, reinterpret_cast<cudaStream_t>(stream), &tp);
+  }
+  FfnTcPlan tplan;
+  if (B <= c->max_tokens && (fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) &&
+      !dev->ffn_tc_off && ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
+      tplan.tiles * tplan.cl <= c->max_ctas) {
+    const wdb::TpArgs tp = make_tp_args(c, B);
+    rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
+                       reinterpret_cast<unsigned long long*>(
+                           sync ? sync : reinterpret_cast<uint32_t*>(dev->ffn_sync)),
+                       y_out, 0, B, E, topk, hidden, inter, status,
+                       reinterpret_cast<cudaStream_t>(stream), &tp);
+    if (rc != WD_ERR_UNSUPPORTED) return rc;
+    dev->ffn_tc_off = true;
+    g_last_error.clear();
   }
   rc = gate_up_impl<wdb::W_BF16>(x, reinterpret_cast<const uint8_t*>(w_gate_up), nullptr,
                                  topk_ids, h_buf, B, E, topk, hidden, inter, status, stream);
