@@ -73,6 +73,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
                    help="N > 1: all-reduce fused into the down kernel, or NCCL after it")
+    p.add_argument("--no-others", action="store_true",
+                   help="skip the BASELINE configs[3] / configs[4] legs (DeepSeek-V3 Zipf, MXFP8)")
     p.add_argument("--no-tp-full", action="store_true",
                    help="skip the BASELINE configs[2] leg (full-width inter 1536 split over the N GPUs)")
     return p.parse_args()
@@ -545,6 +547,10 @@ def run_ours(args, rank, local_rank, world):
                          ", x / topk_ids / topk_scale copied in from one pinned host buffer and y "
                          "copied out inside the timed window, L2 flushed before each call"}
 
+    others = None
+    if world == 1 and args.workload == WORKLOAD and not args.no_extras and not args.no_others:
+        others = run_other_workloads_leg(args, dev, flush, stream, cur, peak_gbs)
+
     tp_full = None
     if args.workload == WORKLOAD and not args.no_extras and not args.no_tp_full:
         for c in cases.values():
@@ -596,6 +602,7 @@ def run_ours(args, rank, local_rank, world):
             "parity": parity,
             "sweep": sweep,
             "tp_full": tp_full,
+            "other_workloads": others,
         }
         print(json.dumps(line), flush=True)
 
@@ -609,6 +616,89 @@ def run_ours(args, rank, local_rank, world):
             fused.close()
         dist.destroy_process_group()
     return 0
+
+
+def cold_us(fn, flush, stream, cur, reps):
+    """Mean cold us of fn(): CUDA graph of one call, L2 flushed before each
+    replay, CUDA events around the replay only."""
+    import numpy as np
+    import torch
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        out = fn()
+    ts = []
+    for _ in range(reps):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        g.replay()
+        b.record(cur)
+        ts.append((a, b))
+    torch.cuda.synchronize()
+    del g, out
+    return float(np.mean([a.elapsed_time(b) for a, b in ts]) * 1000.0)
+
+
+def run_other_workloads_leg(args, dev, flush, stream, cur, peak_gbs):
+    """BASELINE configs[3] (DeepSeek-V3 TP=8 shard, Zipf routing) and
+    configs[4] (Qwen3-30B-A3B with MXFP8 weights, next to the same shape in
+    bf16) after the headline, one GPU: cold us per call through the public
+    API at each of the config's batch sizes, and the fraction of measured HBM
+    on the call's algorithmic bytes.  Reported beside the headline; it does
+    not change `value`."""
+    import torch
+
+    from warp_decode_b200 import warp_decode as wd
+    from warp_decode_b200 import workloads as W
+    from warp_decode_b200.mxfp8 import quantize_mxfp8
+
+    reps = max(5, min(args.kernel_reps, 20))
+    out = {}
+
+    def leg(name, weights, make_call, bf16_w=None):
+        cfg = W.CONFIGS[name]
+        H, I, E, K = cfg.hidden, cfg.inter, cfg.E, cfg.topk
+        rows = []
+        for B in cfg.batches:
+            x, ids, scale = W.make_device_activations(B, H, E, K, cfg.routing, args.seed + 700 + B,
+                                                      device=dev)
+            U = W.unique_experts(ids.cpu().numpy())
+            nb = W.algorithmic_bytes(U, B, H, I, K, weights)["e2e"]
+            us = cold_us(make_call(x, ids, scale), flush, stream, cur, reps)
+            row = {"B": B, "us": round(us, 2), "unique_experts": U, "bytes": nb,
+                   "hbm_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 3)}
+            if bf16_w is not None:
+                wgu, wdn = bf16_w
+                row["bf16_us_same_shape"] = round(
+                    cold_us(lambda: wd.moe_ffn_3d_batched(x, wgu, wdn, ids, scale), flush, stream,
+                            cur, reps), 2)
+            rows.append(row)
+        return {"config": name, "hidden": H, "inter": I, "experts": E, "topk": K,
+                "routing": cfg.routing, "weights": weights, "unit": UNIT,
+                "timing": f"cold (L2 flushed), CUDA graph replay, CUDA events, mean of {reps} calls",
+                "per_batch": rows}
+
+    c = W.CONFIGS["dsv3_tp8"]
+    wgu, wdn = W.make_device_weights(c.hidden, c.inter, c.E, args.seed + 3, device=dev)
+    out["dsv3_tp8"] = leg("dsv3_tp8", "bf16", lambda x, ids, sc: (
+        lambda: wd.moe_ffn_3d_batched(x, wgu, wdn, ids, sc)))
+    del wgu, wdn
+    torch.cuda.empty_cache()
+    c = W.CONFIGS["qwen3_30b_mxfp8"]
+    wgu, wdn = W.make_device_weights(c.hidden, c.inter, c.E, args.seed + 5, device=dev)
+    gq, gs = quantize_mxfp8(wgu)
+    dq, ds = quantize_mxfp8(wdn)
+    out["qwen3_30b_mxfp8"] = leg("qwen3_30b_mxfp8", "mxfp8", lambda x, ids, sc: (
+        lambda: wd.moe_down_3d_batched_mxfp8(wd.moe_gate_up_3d_batched_mxfp8(x, gq, gs, ids),
+                                             dq, ds, ids, sc, x.shape[0])), bf16_w=(wgu, wdn))
+    del wgu, wdn, gq, gs, dq, ds
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_tp_full_leg(args, rank, local_rank, world, dev, flush, stream, cur, fused, peak_gbs):

@@ -179,8 +179,9 @@ WD_API int wd_set_down_path(int path);
  * the call fitting in shared memory (E <= 1024 when B*topk > 1) it is ONE
  * cooperative launch of one CTA per SM (SIMT): the down weights stream while
  * gate_up still computes, and a grid barrier orders h.  For larger calls
- * (automatic choice: B*topk >= 65, B <= 64, inter <= 2048) it is ONE
- * cooperative launch on the tensor cores: the bodies of the two tcgen05
+ * (automatic choice: B*topk >= 65, B <= 64, inter <= 256 and at least 120
+ * CTAs of row-tile clusters, e.g. hidden 4096; forced: inter <= 2048) it is
+ * ONE cooperative launch on the tensor cores: the bodies of the two tcgen05
  * kernels one after the other on the down kernel's clusters, the routing
  * computed once, each CTA streaming its first down weights as soon as its
  * gate_up items are done, and a grid barrier before h is read.  Otherwise it
@@ -294,7 +295,7 @@ WD_API int wd_moe_down_3d_batched_allreduce(const void* h, const void* w_down,
  * in the reference): this rank's gate_up / down shards, then y_out = bf16
  * sum over all ranks (identical bits on every rank).  Where one of the single
  * launches of wd_moe_ffn_3d_batched applies (SIMT: B*topk <= 32
- * automatically; tensor cores: B*topk >= 65; both with B <= the
+ * automatically; tensor cores: as for wd_moe_ffn_3d_batched; both with B <= the
  * communicator's max_tokens) that one cooperative kernel also does the
  * exchange; otherwise gate_up, then wd_moe_down_3d_batched_allreduce.
  * h_buf / sync as for wd_moe_ffn_3d_batched; collective rules as above.

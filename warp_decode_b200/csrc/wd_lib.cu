@@ -1129,6 +1129,16 @@ struct FfnTcPlan {
   int dn_stages = 0, dn_sc = 0, dn_nb = 0;
 };
 
+// The automatic choice takes it from WD_FFN_TC_MIN_SLOTS routed slots and
+// only where its grid is near the SM count and the down items are
+// one weight stage (inter <= 256).  Measured against the two kernels (cold,
+// us): H 7168 (56 tiles x clusters of 2 = 112 CTAs), I 256, B = 32: 207.2 vs
+// 190.5; H 2048, I 768, B = 16: 309.5 vs 195; H 4096, I 1536, B = 16 / 64:
+// 538.6 / 751.5 vs 508.0 / 728.7.
+bool ffn_tc_auto(const FfnTcPlan& p, int B, int topk, int inter) {
+  return B * topk >= WD_FFN_TC_MIN_SLOTS && inter <= 256 && p.tiles * p.cl >= 120;
+}
+
 // Largest cluster size cl <= 8 such that the tiles x cl CTAs of
 // moe_ffn_tc_kernel with `smem` bytes are all resident at once (the grid
 // barrier needs them co-resident); 0 if none.  Cached per device and smem.
@@ -1521,8 +1531,9 @@ int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_do
                       out_fp32, B, E, topk, hidden, inter,
                       status, reinterpret_cast<cudaStream_t>(stream));
   FfnTcPlan tplan;
-  if ((fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) && !dev->ffn_tc_off &&
-      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan)) {
+  if ((fp == 3 || fp == 0) && !dev->ffn_tc_off &&
+      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
+      (fp == 3 || ffn_tc_auto(tplan, B, topk, inter))) {
     rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
                        reinterpret_cast<unsigned long long*>(bar), y_out, out_fp32, B, E, topk,
                        hidden, inter, status, reinterpret_cast<cudaStream_t>(stream));
@@ -1576,8 +1587,9 @@ int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, const vo
                       out_fp32, B, E, topk, hidden, inter, status,
                       reinterpret_cast<cudaStream_t>(stream));
   FfnTcPlan tplan;
-  if ((fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) && !dev->ffn_tc_off &&
-      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan)) {
+  if ((fp == 3 || fp == 0) && !dev->ffn_tc_off &&
+      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
+      (fp == 3 || ffn_tc_auto(tplan, B, topk, inter))) {
     rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
                        reinterpret_cast<unsigned long long*>(sync), y_out, out_fp32, B, E, topk,
                        hidden, inter, status, reinterpret_cast<cudaStream_t>(stream));
@@ -1738,9 +1750,9 @@ int wd_moe_ffn_3d_batched_allreduce(const void* x, const void* w_gate_up, const 
                       topk, hidden, inter, status, reinterpret_cast<cudaStream_t>(stream), &tp);
   }
   FfnTcPlan tplan;
-  if (B <= c->max_tokens && (fp == 3 || (fp == 0 && B * topk >= WD_FFN_TC_MIN_SLOTS)) &&
-      !dev->ffn_tc_off && ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
-      tplan.tiles * tplan.cl <= c->max_ctas) {
+  if (B <= c->max_tokens && (fp == 3 || fp == 0) && !dev->ffn_tc_off &&
+      ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
+      (fp == 3 || ffn_tc_auto(tplan, B, topk, inter)) && tplan.tiles * tplan.cl <= c->max_ctas) {
     const wdb::TpArgs tp = make_tp_args(c, B);
     rc = ffn_tc_launch(dev, tplan, x, w_gate_up, w_down, topk_ids, topk_scale, h_buf,
                        reinterpret_cast<unsigned long long*>(
