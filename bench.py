@@ -73,6 +73,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
                    help="N > 1: all-reduce fused into the down kernel, or NCCL after it")
+    p.add_argument("--profile-once", action="store_true",
+                   help="one eager e2e call per batch size, no timing (for ncu captures)")
     p.add_argument("--no-others", action="store_true",
                    help="skip the BASELINE configs[3] / configs[4] legs (DeepSeek-V3 Zipf, MXFP8)")
     p.add_argument("--no-tp-full", action="store_true",
@@ -353,6 +355,19 @@ def run_ours(args, rank, local_rank, world):
             return fused.ffn(c.x, w_gu, w_dn, c.ids, c.scale)
         return nccl_call(c)
 
+    if args.profile_once:
+        # One eager call per batch size and nothing else (profiler captures:
+        # the k-th launch of a kernel is the k-th batch size's call).
+        for B in batches:
+            e2e_call(cases[B])
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+            if fused is not None:
+                fused.close()
+            dist.destroy_process_group()
+        return 0
+
     # Correctness of the timed path before timing it (every rank, same order).
     parity = None
     if not mx:
@@ -470,25 +485,53 @@ def run_ours(args, rank, local_rank, world):
                 "published_h20_hot_e2e_us": (PUBLISHED_H20_E2E_US.get(B)
                                              if args.workload == WORKLOAD else None),
             })
-        achieved = gu_bytes / (gu_time * 1e-6) / 1e9
+        # Roofline of the dominant kernel of the e2e path: the kernel choice
+        # of each call (wd_moe_ffn_3d_batched_kernels), its share of the
+        # sweep's time; a single-launch choice is one kernel, so its CUDA-event
+        # time is that kernel's launch duration and its bytes the call's.
+        from warp_decode_b200 import capi
+
+        kinds = {}
+        if world == 1 and not mx:
+            for B in batches:
+                kinds[B] = capi.ffn_kernels(B, E, K, H, I)
+        share = {}
+        for B, k in kinds.items():
+            share[k] = share.get(k, 0.0) + per_b_us[B]
+        dom = max(share, key=share.get) if share else None
         traffic = None
-        tpath = ROOT / "profiles" / "gate_up_dram_traffic.json"
-        if tpath.exists() and args.workload == WORKLOAD:
+        if dom in (capi.FFN_KERNELS_TC_SINGLE, capi.FFN_KERNELS_SIMT_SINGLE):
+            bs = [B for B in batches if kinds[B] == dom]
+            kbytes = sum(cases[B].bytes["e2e"] for B in bs)
+            ktime = sum(per_b_us[B] for B in bs)
+            kname = ("moe_ffn_tc_kernel (tensor-core single launch)"
+                     if dom == capi.FFN_KERNELS_TC_SINGLE else "moe_ffn_kernel (SIMT single launch)")
+            fname = "ffn_tc_dram_traffic.json" if dom == capi.FFN_KERNELS_TC_SINGLE else None
+            method = (f"sum of algorithmic e2e bytes over the calls this kernel serves (B = "
+                      f"{', '.join(map(str, bs))}; one launch each) / sum of their cold CUDA-event "
+                      f"durations; {100.0 * ktime / sum(per_b_us.values()):.0f} % of the sweep's time")
+        else:
+            bs = list(batches)
+            kbytes, ktime = gu_bytes, gu_time
+            kname = ("gate_up (moe_gate_up_kernel<e4m3>, MXFP8 weights)" if mx else
+                     "gate_up (moe_gate_up_kernel B<16, moe_gate_up_tc_kernel B>=16)")
+            fname = None
+            method = ("sum of algorithmic gate_up bytes over the sweep / sum of cold per-launch "
+                      "CUDA-event durations (one launch per batch size)")
+        achieved = kbytes / (ktime * 1e-6) / 1e9
+        if fname and (ROOT / "profiles" / fname).exists() and args.workload == WORKLOAD:
             try:
-                t = json.loads(tpath.read_text())
-                per = [t["per_batch"][str(B)] for B in batches if str(B) in t["per_batch"]]
-                if len(per) == nB:
-                    traffic = sum(per) / nB
+                t = json.loads((ROOT / "profiles" / fname).read_text())
+                per = [t["per_batch"][str(B)] for B in bs if str(B) in t["per_batch"]]
+                if len(per) == len(bs):
+                    traffic = sum(per) / len(bs)
             except Exception:
                 traffic = None
-        kname = ("gate_up (moe_gate_up_kernel<e4m3>, MXFP8 weights)" if mx else
-                 "gate_up (moe_gate_up_kernel B<16, moe_gate_up_tc_kernel B>=16)")
         roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                     "peak": peak_gbs, "peak_kind": peak_kind, "unit": "GB/s",
                     "frac": round(achieved / peak_gbs, 4),
-                    "alg_bytes_per_launch": gu_bytes / nB, "traffic": traffic,
-                    "method": "sum of algorithmic gate_up bytes over the sweep / sum of cold "
-                              "per-launch CUDA-event durations (one launch per batch size)"}
+                    "alg_bytes_per_launch": kbytes / len(bs), "traffic": traffic,
+                    "method": method}
 
         # ---- end to end through the public API with host buffers ----
         # x, topk_ids and topk_scale of a call sit in one pinned host buffer

@@ -250,6 +250,18 @@ WD_API int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk
 WD_API int wd_set_ffn_path(int path);
 
 /*
+ * Which kernels wd_moe_ffn_3d_batched (and its _noalloc twin) would run for
+ * these sizes on the current device with the current choice: *kind =
+ * WD_FFN_KERNELS_SPLIT (gate_up then down), _SIMT_SINGLE (one SIMT launch)
+ * or _TC_SINGLE (one tensor-core launch).  Launches nothing.  No counterpart
+ * in the reference.
+ */
+#define WD_FFN_KERNELS_SPLIT 0
+#define WD_FFN_KERNELS_SIMT_SINGLE 1
+#define WD_FFN_KERNELS_TC_SINGLE 2
+WD_API int wd_moe_ffn_3d_batched_kernels(int B, int E, int topk, int hidden, int inter, int* kind);
+
+/*
  * Tensor parallelism over `inter` with the all-reduce fused into down (no
  * counterpart in the reference, which has no multi-GPU path).  One process
  * per GPU; every rank of a group of `world` (2..8) ranks:

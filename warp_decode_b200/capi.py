@@ -48,6 +48,7 @@ _SIGS = {
     "wd_moe_ffn_3d_batched": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                    _P]),
     "wd_set_ffn_path": (_I, [_I]),
+    "wd_moe_ffn_3d_batched_kernels": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
     "wd_moe_ffn_3d_batched_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                            _P]),
     "wd_moe_router_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P]),
@@ -139,6 +140,17 @@ def router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize, stre
 def set_ffn_path(path: int) -> None:
     """Select the kernels behind wd_moe_ffn_3d_batched (FFN_AUTO / _SPLIT / _FUSED / _TC)."""
     check(lib().wd_set_ffn_path(int(path)))
+
+
+# Values of ffn_kernels.
+FFN_KERNELS_SPLIT, FFN_KERNELS_SIMT_SINGLE, FFN_KERNELS_TC_SINGLE = 0, 1, 2
+
+
+def ffn_kernels(B: int, E: int, topk: int, hidden: int, inter: int) -> int:
+    """Which kernels wd_moe_ffn_3d_batched would run for these sizes (FFN_KERNELS_*)."""
+    kind = ctypes.c_int(-1)
+    check(lib().wd_moe_ffn_3d_batched_kernels(B, E, topk, hidden, inter, ctypes.byref(kind)))
+    return int(kind.value)
 
 
 def set_gate_up_path(path: int) -> None:

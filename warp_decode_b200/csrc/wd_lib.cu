@@ -1503,6 +1503,29 @@ int wd_set_ffn_path(int path) {
   return WD_OK;
 }
 
+int wd_moe_ffn_3d_batched_kernels(int B, int E, int topk, int hidden, int inter, int* kind) {
+  g_last_error.clear();
+  if (!kind) return fail(WD_ERR_NULL_POINTER, "kind is NULL");
+  int rc = check_common(B, E, topk, hidden, inter);
+  if (rc) return rc;
+  *kind = WD_FFN_KERNELS_SPLIT;
+  if (B == 0) return WD_OK;
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  const int fp = ffn_path();
+  FfnPlan plan;
+  FfnTcPlan tplan;
+  if ((fp == 0 || fp == 2) &&
+      ffn_plan(dev, B, E, topk, hidden, inter,
+               fp == 2 ? wdb::FFN_MAX_SLOTS : WD_FFN_AUTO_MAX_SLOTS, &plan))
+    *kind = WD_FFN_KERNELS_SIMT_SINGLE;
+  else if ((fp == 3 || fp == 0) && !dev->ffn_tc_off &&
+           ffn_tc_plan(dev, B, E, topk, hidden, inter, &tplan) &&
+           (fp == 3 || ffn_tc_auto(tplan, B, topk, inter)))
+    *kind = WD_FFN_KERNELS_TC_SINGLE;
+  return WD_OK;
+}
+
 int wd_moe_ffn_3d_batched(const void* x, const void* w_gate_up, const void* w_down,
                           const int32_t* topk_ids, const float* topk_scale, void* h_buf,
                           uint32_t* sync, void* y_out, int out_fp32, int B, int E, int topk,
