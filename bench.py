@@ -392,7 +392,11 @@ def run_ours(args, rank, local_rank, world):
         c.g_e2e, c.y, launches[c.B] = capture(lambda c=c: e2e_call(c))
         c.g_gu, c.h, _ = capture(lambda c=c: gate_up(c.x, c.ids))
         c.g_dn, _, _ = capture(lambda c=c: down(c.h, c.ids, c.scale, c.B))
-        c.g_split = None
+        c.g_split = c.g_nccl = None
+        if world > 1 and not args.no_extras:
+            # the unfused path of the same call (partial down, NCCL all-reduce,
+            # bf16 cast) for the per-B fused-vs-NCCL comparison
+            c.g_nccl, _, _ = capture(lambda c=c: nccl_call(c))
         if world == 1 and not mx:
             c.g_split, _, _ = capture(lambda c=c: down(gate_up(c.x, c.ids), c.ids, c.scale, c.B))
     torch.cuda.synchronize()
@@ -470,6 +474,7 @@ def run_ours(args, rank, local_rank, world):
             t_dn = cold_time(c.g_dn, args.kernel_reps)
             t_hot = hot_time(c.g_e2e, args.hot_iters)
             t_split = cold_time(c.g_split, args.kernel_reps) if c.g_split is not None else None
+            t_nccl = cold_time(c.g_nccl, args.kernel_reps) if c.g_nccl is not None else None
             gu_bytes += c.bytes["gate_up"]
             gu_time += t_gu
             sweep.append({
@@ -477,6 +482,8 @@ def run_ours(args, rank, local_rank, world):
                 "e2e_launches": launches[B],
                 "e2e_hot_us": round(t_hot, 2), "gate_up_us": round(t_gu, 2), "down_us": round(t_dn, 2),
                 "two_call_e2e_us": round(t_split, 2) if t_split is not None else None,
+                "nccl_e2e_us": round(t_nccl, 2) if t_nccl is not None else None,
+                "exchange": exchange_record(fused, B, H, world),
                 "bytes_e2e": c.bytes["e2e"],
                 "e2e_tbs": round(c.bytes["e2e"] / (per_b_us[B] * 1e-6) / 1e12, 3),
                 "e2e_frac": round(c.bytes["e2e"] / (per_b_us[B] * 1e-6) / 1e9 / peak_gbs, 3),
@@ -547,31 +554,67 @@ def run_ours(args, rank, local_rank, world):
             xd = dbuf[:xb].view(torch.bfloat16).view(B, H)
             idd = dbuf[xb:xb + ib].view(torch.int32).view(B, K)
             scd = dbuf[xb + ib:].view(torch.float32).view(B, K)
-            packed[B] = (host, dbuf, xd, idd, scd, torch.empty(B, H, dtype=torch.bfloat16).pin_memory())
+            xh = host[:xb].view(torch.bfloat16).view(B, H)
+            idh = host[xb:xb + ib].view(torch.int32).view(B, K)
+            sch = host[xb + ib:].view(torch.float32).view(B, K)
+            packed[B] = (host, dbuf, xd, idd, scd, torch.empty(B, H, dtype=torch.bfloat16).pin_memory(),
+                         (xh, idh, sch))
         h2d = sum(B * H * 2 + B * K * 8 for B in batches)
         d2h = sum(B * H * 2 for B in batches)
         reps = max(5, min(args.steps, 30))
+
+        def api_call(B, xd, idd, scd):
+            if world == 1:
+                return ffn(xd, idd, scd)
+            if fused is not None and fused.applies(B):
+                return fused.ffn(xd, w_gu, w_dn, idd, scd)
+            h = wd.moe_gate_up_3d_batched(xd, w_gu, idd)
+            y = wd.moe_down_3d_batched_partial(h, w_dn, idd, scd, B)
+            dist.all_reduce(y)
+            return y.to(torch.bfloat16)
+
+        def e2e_step(B):
+            """One step through the public API with host buffers: inputs in
+            and y out by the library's copy kernel (wd_copy_ranges), the FFN
+            between (moe_ffn_3d_batched_host does all three at N = 1)."""
+            host, dbuf, xd, idd, scd, yh, (xh, idh, sch) = packed[B]
+            if world == 1 and not mx:
+                return wd.moe_ffn_3d_batched_host(xh, w_gu, w_dn, idh, sch, out=yh)
+            wd.copy_ranges([host], [dbuf])
+            y = api_call(B, xd, idd, scd)
+            wd.copy_ranges([y], [yh])
+            return yh
+
+        def timed(fn):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            fn()
+            b.record(cur)
+            return a, b
+
+        # Per call, cold timings of the same step (L2 flushed first): the e2e
+        # step itself and, at N = 1, its parts: the two transfers alone by the
+        # copy kernel and by the copy engine (non_blocking torch copies: the
+        # packed inputs in, a [B, H] bf16 buffer out), and the eager API call
+        # alone on device-resident inputs.  Only the first enters `value`.
         e2e_ts = []
+        parts_ts = {B: {"copies": [], "copies_dma": [], "eager_call": []} for B in batches}
         for r in range(reps + 2):
             row = []
             for B in batches:
-                host, dbuf, xd, idd, scd, yh = packed[B]
-                flush()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(cur)
-                dbuf.copy_(host, non_blocking=True)
+                host, dbuf, xd, idd, scd, yh, _ = packed[B]
+                row.append(timed(lambda: e2e_step(B)))
                 if world == 1:
-                    y = ffn(xd, idd, scd)
-                elif fused is not None and fused.applies(B):
-                    y = fused.ffn(xd, w_gu, w_dn, idd, scd)
-                else:
-                    h = wd.moe_gate_up_3d_batched(xd, w_gu, idd)
-                    y = wd.moe_down_3d_batched_partial(h, w_dn, idd, scd, B)
-                    dist.all_reduce(y)
-                    y = y.to(torch.bfloat16)
-                yh.copy_(y, non_blocking=True)
-                b.record(cur)
-                row.append((a, b))
+                    y = cases[B].y
+                    ev = {"copies": timed(lambda: (wd.copy_ranges([host], [dbuf]),
+                                                   wd.copy_ranges([y], [yh]))),
+                          "copies_dma": timed(lambda: (dbuf.copy_(host, non_blocking=True),
+                                                       yh.copy_(y, non_blocking=True))),
+                          "eager_call": timed(lambda: api_call(B, xd, idd, scd))}
+                    if r >= 2:
+                        for k, v in ev.items():
+                            parts_ts[B][k].append(v)
             if r >= 2:
                 e2e_ts.append(row)
         torch.cuda.synchronize()
@@ -579,16 +622,32 @@ def run_ours(args, rank, local_rank, world):
                                  dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+        breakdown = None
+        if world == 1:
+            breakdown = []
+            for i, B in enumerate(batches):
+                ev = lambda lst: round(float(np.mean([a.elapsed_time(b) for a, b in lst])) * 1000.0, 2)
+                breakdown.append({"B": B,
+                                  "e2e_us": round(float(np.mean([row[i][0].elapsed_time(row[i][1])
+                                                                 for row in e2e_ts])) * 1000.0, 2),
+                                  "copies_us": ev(parts_ts[B]["copies"]),
+                                  "copies_dma_us": ev(parts_ts[B]["copies_dma"]),
+                                  "eager_call_us": ev(parts_ts[B]["eager_call"]),
+                                  "graph_call_us": round(per_b_us[B], 2),
+                                  "h2d_bytes": B * H * 2 + B * K * 8, "d2h_bytes": B * H * 2})
         e2e = {"value": round(float(e2e_total.item()) * 1000.0 / (len(e2e_ts) * nB), 3), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "method": ("eager torch API (moe_ffn_3d_batched) per call"
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "breakdown": breakdown,
+               "method": ("eager torch API (moe_ffn_3d_batched_host) per call"
                           if world == 1 and not mx else
-                          "eager torch API (moe_gate_up_3d_batched_mxfp8 + moe_down_3d_batched_mxfp8) per call"
+                          "eager torch API (copy_ranges, moe_gate_up_3d_batched_mxfp8 + "
+                          "moe_down_3d_batched_mxfp8, copy_ranges) per call"
                           if world == 1 else
-                          "eager torch API (FusedAllReduce.ffn, or moe_gate_up_3d_batched + "
-                          "moe_down_3d_batched_partial + all_reduce above the fused size) per call") +
-                         ", x / topk_ids / topk_scale copied in from one pinned host buffer and y "
-                         "copied out inside the timed window, L2 flushed before each call"}
+                          "eager torch API (copy_ranges, FusedAllReduce.ffn or moe_gate_up_3d_batched + "
+                          "moe_down_3d_batched_partial + all_reduce above the fused size, copy_ranges) "
+                          "per call") +
+                         ": x / topk_ids / topk_scale from pinned host memory in and y to pinned host "
+                         "memory out by the library's copy kernel inside the timed window, L2 flushed "
+                         "before each call"}
 
     others = None
     if world == 1 and args.workload == WORKLOAD and not args.no_extras and not args.no_others:
@@ -597,7 +656,7 @@ def run_ours(args, rank, local_rank, world):
     tp_full = None
     if args.workload == WORKLOAD and not args.no_extras and not args.no_tp_full:
         for c in cases.values():
-            del c.g_e2e, c.g_gu, c.g_dn, c.g_split
+            del c.g_e2e, c.g_gu, c.g_dn, c.g_split, c.g_nccl
         torch.cuda.empty_cache()
         tp_full = run_tp_full_leg(args, rank, local_rank, world, dev, flush, stream, cur,
                                   fused, peak_gbs)
@@ -651,7 +710,7 @@ def run_ours(args, rank, local_rank, world):
 
     if tp_full is None:
         for c in cases.values():
-            del c.g_e2e, c.g_gu, c.g_dn, c.g_split
+            del c.g_e2e, c.g_gu, c.g_dn, c.g_split, c.g_nccl
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -659,6 +718,19 @@ def run_ours(args, rank, local_rank, world):
             fused.close()
         dist.destroy_process_group()
     return 0
+
+
+def exchange_record(fused, B, H, world):
+    """NVLink bytes one rank sends in the fused exchange of a [B, H] call
+    (8-byte packets: one-shot pushes every partial row to every peer;
+    two-shot pushes each row to its owner and the owner's bf16 result back),
+    or None where the call is not fused."""
+    if world == 1 or fused is None or not fused.applies(B):
+        return None
+    one_shot = B * H * 8 * (world - 1)
+    two_shot = world >= 4 and one_shot > int(os.environ.get("WARP_DECODE_TP_TWO_SHOT_BYTES") or 512 << 10)
+    sent = 2 * B * H * 8 * (world - 1) // world if two_shot else one_shot
+    return {"shape": "two-shot" if two_shot else "one-shot", "bytes_sent_per_rank": sent}
 
 
 def cold_us(fn, flush, stream, cur, reps):
@@ -922,9 +994,72 @@ def run_reference(args, rank, world):
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "per_batch_us": r["per_batch_us"],
+        "reference_gpu_kernels": (reference_gpu_kernels_leg(args, batches)
+                                  if world == 1 and args.workload == WORKLOAD else None),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_gpu_kernels_leg(args, batches):
+    """The reference's own CUDA kernels (csrc/*.cu, rebuilt unmodified for
+    sm_100a into oracle/_ref/ by oracle/Makefile) on this GPU, by the method
+    of the headline: gate_up + down of each batch size in one CUDA graph, L2
+    flushed before each replay, CUDA events around the replay, the headline's
+    inputs (same seeds); beside them this library's e2e call timed the same
+    way.  A same-box GPU bar for the headline, reported with the reference
+    arm; None where no GPU or no rebuilt library is present."""
+    import ctypes
+
+    try:
+        import torch
+    except Exception:
+        return None
+    lib_path = ROOT / "oracle" / "_ref" / "libwdref.so"
+    if not torch.cuda.is_available() or not lib_path.exists():
+        return None
+    from warp_decode_b200 import warp_decode as wd
+    from warp_decode_b200 import workloads as W
+
+    L = ctypes.CDLL(str(lib_path))
+    P, I_ = ctypes.c_void_p, ctypes.c_int
+    L.wdref_gate_up.argtypes = [P, P, P, P, I_, I_, I_, I_, I_, P]
+    L.wdref_down.argtypes = [P, P, P, P, P, I_, I_, I_, I_, I_, P]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = W.CONFIGS[WORKLOAD]
+    H, I, E, K = cfg.hidden, cfg.inter, cfg.E, cfg.topk
+    w_gu, w_dn = W.make_device_weights(H, I, E, args.seed, device=dev)
+    flush = L2Flush(dev)
+    stream = torch.cuda.Stream(device=dev)
+    cur = torch.cuda.current_stream(dev)
+    reps = max(5, min(args.kernel_reps, 20))
+    rows = []
+    for B in batches:
+        x, ids, scale = W.make_device_activations(B, H, E, K, cfg.routing, args.seed + B, device=dev)
+        h = torch.empty(B * K, I, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+
+        def ref_e2e():
+            st = torch.cuda.current_stream().cuda_stream
+            L.wdref_gate_up(x.data_ptr(), w_gu.data_ptr(), ids.data_ptr(), h.data_ptr(), B, E, K,
+                            H, I, st)
+            L.wdref_down(h.data_ptr(), w_dn.data_ptr(), ids.data_ptr(), scale.data_ptr(),
+                         y.data_ptr(), B, E, K, H, I, st)
+
+        ref = cold_us(ref_e2e, flush, stream, cur, reps)
+        ours = cold_us(lambda: wd.moe_ffn_3d_batched(x, w_gu, w_dn, ids, scale), flush, stream,
+                       cur, reps)
+        rows.append({"B": B, "reference_kernels_us": round(ref, 2), "ours_us": round(ours, 2),
+                     "speedup": round(ref / ours, 2)})
+    del w_gu, w_dn
+    torch.cuda.empty_cache()
+    return {"what": "csrc/moe_gate_up_3d_batched.cu + csrc/moe_down_3d_batched.cu of the "
+                    "reference, compiled unmodified for sm_100a, two launches per call",
+            "timing": f"cold (L2 flushed), CUDA graph replay, CUDA events, mean of {reps} calls",
+            "unit": UNIT, "per_batch": rows,
+            "mean_reference_kernels_us": round(sum(r["reference_kernels_us"] for r in rows) / len(rows), 3),
+            "mean_ours_us": round(sum(r["ours_us"] for r in rows) / len(rows), 3)}
 
 
 def main():

@@ -48,6 +48,7 @@
 #ifndef WARP_DECODE_B200_H_
 #define WARP_DECODE_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__) || defined(__clang__)
@@ -238,6 +239,25 @@ WD_API int wd_moe_ffn_3d_batched_noalloc(const void* x, const void* w_gate_up, c
 WD_API int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
                               float* topk_weights, int B, int E, int topk, int renormalize,
                               void* stream);
+
+/*
+ * Host <-> device transfers of a decode step by the GPU's own loads and
+ * stores, in one launch on `stream` (no copy engine): for i < n, bytes[i]
+ * bytes from src[i] to dst[i].  No counterpart in the reference, whose API
+ * takes device tensors only; this is how a caller holding x / topk_ids /
+ * topk_scale in host memory moves them in, and y out, around
+ * wd_moe_ffn_3d_batched (the copy engine's fixed start-up cost dominates
+ * transfers of a few KB to a few hundred KB).  Each pointer is memory of the
+ * current device or page-locked host memory (cudaHostAlloc, or registered
+ * with cudaHostRegister); pageable host memory, or another device's memory,
+ * is refused with WD_ERR_UNSUPPORTED before anything is launched.  Ranges
+ * must not overlap.  1 <= n <= 4 (n = 0 and empty ranges are no-ops); any
+ * alignment (16-byte aligned ranges move in 16-byte units).  Asynchronous:
+ * the host may read a dst in host memory once the stream has passed the
+ * launch (event or stream synchronisation).
+ */
+WD_API int wd_copy_ranges(const void* const* src, void* const* dst, const size_t* bytes, int n,
+                          void* stream);
 
 /*
  * Kernel choice behind wd_moe_ffn_3d_batched for later calls in this process:

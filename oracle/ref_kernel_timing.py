@@ -107,7 +107,7 @@ def main():
             return wd.moe_down_3d_batched(h_r, w_dn, ids, scale, B)
 
         def our_e2e():
-            return wd.moe_down_3d_batched(wd.moe_gate_up_3d_batched(x, w_gu, ids), w_dn, ids, scale, B)
+            return wd.moe_ffn_3d_batched(x, w_gu, w_dn, ids, scale)
 
         U = W.unique_experts(ids.cpu().numpy())
         row = {"B": B, "unique_experts": U, "bytes": W.algorithmic_bytes(U, B, H, I, K)}

@@ -15,7 +15,7 @@ from warp_decode_b200 import capi, _build
 
 def test_library_exports_every_header_symbol():
     names = capi.header_symbols()
-    assert len(names) == 22, names
+    assert len(names) == 23, names
     L = capi.lib()
     for n in names:
         assert hasattr(L, n), n

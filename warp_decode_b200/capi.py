@@ -52,6 +52,8 @@ _SIGS = {
     "wd_moe_ffn_3d_batched_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P,
                                            _P]),
     "wd_moe_router_topk": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P]),
+    "wd_copy_ranges": (_I, [ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t),
+                            _I, _P]),
     "wd_moe_ffn_3d_batched_allreduce": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                                              _P, _P, _P]),
 }
@@ -135,6 +137,15 @@ def ffn_noalloc(x, w_gu, w_dn, ids, scale, out, out_fp32, B, E, topk, hidden, in
 def router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize, stream=0) -> int:
     return lib().wd_moe_router_topk(logits, logits_fp32, ids, weights, B, E, topk, renormalize,
                                     stream)
+
+
+def copy_ranges(src, dst, nbytes, stream=0) -> int:
+    """wd_copy_ranges over parallel lists of addresses (ints) and byte counts."""
+    n = len(src)
+    sp = (_P * max(n, 1))(*src)
+    dp = (_P * max(n, 1))(*dst)
+    nb = (ctypes.c_size_t * max(n, 1))(*nbytes)
+    return lib().wd_copy_ranges(sp, dp, nb, n, stream)
 
 
 def set_ffn_path(path: int) -> None:

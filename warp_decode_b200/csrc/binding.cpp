@@ -197,6 +197,88 @@ torch::Tensor moe_ffn_3d_batched(torch::Tensor x, torch::Tensor w_gate_up, torch
   return out;
 }
 
+// Byte copies src[i] -> dst[i] (1-4 pairs of contiguous tensors of equal
+// byte size) by the GPU's own loads and stores, one launch on the current
+// stream of the pairs' CUDA device; host tensors must be pinned.
+void copy_ranges(const std::vector<torch::Tensor>& src, const std::vector<torch::Tensor>& dst) {
+  TORCH_CHECK(!src.empty() && src.size() == dst.size() && src.size() <= 4,
+              "copy_ranges takes 1-4 (src, dst) pairs");
+  c10::optional<at::Device> dev;
+  const void* sp[4];
+  void* dp[4];
+  size_t nb[4];
+  for (size_t i = 0; i < src.size(); ++i) {
+    for (const torch::Tensor* t : {&src[i], &dst[i]}) {
+      CHECK_CONTIG(*t);
+      if (t->is_cuda()) {
+        TORCH_CHECK(!dev || *dev == t->device(), "copy_ranges: CUDA tensors on more than one device");
+        dev = t->device();
+      } else {
+        TORCH_CHECK(t->device().is_cpu() && (t->numel() == 0 || t->is_pinned()),
+                    "copy_ranges: host tensors must be pinned");
+      }
+    }
+    TORCH_CHECK(src[i].nbytes() == dst[i].nbytes(), "copy_ranges: src and dst sizes differ");
+    sp[i] = src[i].data_ptr();
+    dp[i] = dst[i].data_ptr();
+    nb[i] = src[i].nbytes();
+  }
+  TORCH_CHECK(dev.has_value(), "copy_ranges: no CUDA tensor names the device");
+  const c10::cuda::CUDAGuard guard(*dev);
+  check_rc(wd_copy_ranges(sp, dp, nb, (int)src.size(), stream_ptr()));
+}
+
+// moe_ffn_3d_batched with x / topk_ids / topk_scale in pinned host memory and
+// y returned in pinned host memory: inputs in (one copy launch), the FFN, y
+// out (one copy launch), all on the current stream of the weights' device.
+// (Storing y straight into the host buffer from the FFN's epilogues measured
+// slower from 8 tokens up: 2-byte stores scattered over PCIe.)  Asynchronous
+// like a non_blocking copy: read y after synchronising.
+torch::Tensor moe_ffn_3d_batched_host(torch::Tensor x, torch::Tensor w_gate_up, torch::Tensor w_down,
+                                      torch::Tensor topk_ids, torch::Tensor topk_scale,
+                                      c10::optional<torch::Tensor> out, bool fp32_out) {
+  for (const torch::Tensor* t : {&x, &topk_ids, &topk_scale}) {
+    TORCH_CHECK(t->device().is_cpu() && (t->numel() == 0 || t->is_pinned()),
+                "x, topk_ids and topk_scale must be pinned host tensors");
+    CHECK_CONTIG(*t);
+  }
+  CHECK_BF16(x); CHECK_I32(topk_ids); CHECK_F32(topk_scale);
+  CHECK_CUDA(w_gate_up);
+  TORCH_CHECK(x.dim() == 2 && topk_ids.dim() == 2 && topk_scale.dim() == 2 &&
+                  topk_ids.size(0) == x.size(0) && topk_scale.sizes() == topk_ids.sizes(),
+              "x must be [B, hidden], topk_ids and topk_scale [B, topk]");
+  const c10::cuda::CUDAGuard guard(w_gate_up.device());
+  const int64_t xb = x.nbytes(), ib = topk_ids.nbytes(), sb = topk_scale.nbytes();
+  const int64_t io = (xb + 15) / 16 * 16, so = io + (ib + 15) / 16 * 16;
+  auto buf = torch::empty({so + sb}, w_gate_up.options().dtype(at::kByte));
+  auto xd = buf.narrow(0, 0, xb).view(at::kBFloat16).view(x.sizes());
+  auto idd = buf.narrow(0, io, ib).view(at::kInt).view(topk_ids.sizes());
+  auto scd = buf.narrow(0, so, sb).view(at::kFloat).view(topk_scale.sizes());
+  {
+    const void* sp[3] = {x.data_ptr(), topk_ids.data_ptr(), topk_scale.data_ptr()};
+    void* dp[3] = {xd.data_ptr(), idd.data_ptr(), scd.data_ptr()};
+    const size_t nb[3] = {(size_t)xb, (size_t)ib, (size_t)sb};
+    check_rc(wd_copy_ranges(sp, dp, nb, 3, stream_ptr()));
+  }
+  const auto ydt = fp32_out ? at::kFloat : at::kBFloat16;
+  torch::Tensor yh;
+  if (out.has_value()) {
+    yh = *out;
+    TORCH_CHECK(yh.device().is_cpu() && (yh.numel() == 0 || yh.is_pinned()) && yh.is_contiguous() &&
+                    yh.scalar_type() == ydt && yh.dim() == 2 && yh.size(0) == x.size(0) &&
+                    yh.size(1) == x.size(1),
+                "out must be a pinned contiguous host tensor [B, hidden] of the output dtype");
+  } else {
+    yh = torch::empty({x.size(0), x.size(1)}, x.options().dtype(ydt).pinned_memory(true));
+  }
+  auto y = moe_ffn_3d_batched(xd, w_gate_up, w_down, idd, scd, fp32_out);
+  const void* sp[1] = {y.data_ptr()};
+  void* dp[1] = {yh.data_ptr()};
+  const size_t nb[1] = {(size_t)y.nbytes()};
+  check_rc(wd_copy_ranges(sp, dp, nb, 1, stream_ptr()));
+  return yh;
+}
+
 // Router producer: (topk_ids int32 [B, topk], topk_weights fp32 [B, topk]).
 std::tuple<torch::Tensor, torch::Tensor> moe_router_topk(torch::Tensor logits, int64_t topk,
                                                          bool renormalize) {
@@ -253,6 +335,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "gate_up + silu*up + down + top-k weighted sum in one call (one launch for B*topk <= 64)",
         py::arg("x"), py::arg("w_gate_up"), py::arg("w_down"), py::arg("topk_ids"),
         py::arg("topk_scale"), py::arg("fp32_out") = false);
+  m.def("copy_ranges", &copy_ranges,
+        "byte copies src[i] -> dst[i] (1-4 pairs; device or pinned host tensors) in one launch",
+        py::arg("src"), py::arg("dst"));
+  m.def("moe_ffn_3d_batched_host", &moe_ffn_3d_batched_host,
+        "moe_ffn_3d_batched on pinned host x / topk_ids / topk_scale, y returned in pinned host memory",
+        py::arg("x"), py::arg("w_gate_up"), py::arg("w_down"), py::arg("topk_ids"),
+        py::arg("topk_scale"), py::arg("out") = py::none(), py::arg("fp32_out") = false);
   m.def("moe_router_topk", &moe_router_topk,
         "top-k experts and routing weights from router logits [B, E] (bf16/fp32)",
         py::arg("logits"), py::arg("topk"), py::arg("renormalize") = true);

@@ -179,9 +179,6 @@ struct TpCall {
     v = __uint_as_float((uint32_t)w);
     return true;
   }
-  // Sum of every rank's partial of (t, row) in rank order (a row this rank
-  // sums; the ranks' packets are read together, then any late one polled);
-  // two-shot also sends the bf16 result to the other ranks.
   // The ranks' packets of (t, row) in this rank's buffer, read together.
   __device__ void peek_all(int t, int row, unsigned long long (&w)[TP_MAX_WORLD]) const {
 #pragma unroll

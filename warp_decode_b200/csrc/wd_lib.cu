@@ -28,6 +28,7 @@
 #include "wd_ffn.cuh"
 #include "wd_ffn_tc.cuh"
 #include "wd_router.cuh"
+#include "wd_copy.cuh"
 
 // Scratch of wd_moe_ffn_3d_batched_noalloc: [0, 8) the grid-barrier counter
 // (zero at module load; each single-launch call adds GRID_BAR_UNITS in total,
@@ -1394,6 +1395,36 @@ wdb::TpArgs make_tp_args(const TpComm* c, int B) {
   return tp;
 }
 
+// Device-visible address of `p` for the current device: device (or managed)
+// memory of this device as is, page-locked host memory through its mapping.
+// Pageable host memory and other devices' memory are refused before anything
+// is launched, so the copy kernel only ever dereferences mapped addresses.
+int device_view(const void* p, int dev, const char* what, unsigned char** out) {
+  cudaPointerAttributes at{};
+  const cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(WD_ERR_CUDA, std::string(what) + ": cudaPointerGetAttributes: " + cudaGetErrorString(e));
+  }
+  switch (at.type) {
+    case cudaMemoryTypeHost:
+      if (!at.devicePointer)
+        return fail(WD_ERR_UNSUPPORTED, std::string(what) + ": page-locked host memory without a device mapping");
+      *out = static_cast<unsigned char*>(at.devicePointer);
+      return WD_OK;
+    case cudaMemoryTypeDevice:
+    case cudaMemoryTypeManaged:
+      if (at.device != dev)
+        return fail(WD_ERR_UNSUPPORTED, std::string(what) + ": memory of another device");
+      *out = static_cast<unsigned char*>(const_cast<void*>(p));
+      return WD_OK;
+    default:
+      return fail(WD_ERR_UNSUPPORTED, std::string(what) +
+                                          ": pageable host memory (the GPU cannot read or write it; "
+                                          "allocate it page-locked or register it)");
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -1491,6 +1522,48 @@ int wd_moe_router_topk(const void* logits, int logits_fp32, int32_t* topk_ids,
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess)
     return fail(WD_ERR_CUDA, std::string("router launch: ") + cudaGetErrorString(err));
+  note_launch();
+  return WD_OK;
+}
+
+int wd_copy_ranges(const void* const* src, void* const* dst, const size_t* bytes, int n,
+                   void* stream) {
+  g_last_error.clear();
+  if (n < 0 || n > wdb::COPY_MAX_RANGES) return fail(WD_ERR_SHAPE, "need 0 <= n <= 4 ranges");
+  if (n > 0 && (!src || !dst || !bytes)) return fail(WD_ERR_NULL_POINTER, "null range array");
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return fail(WD_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+  wdb::CopyRanges c{};
+  c.first[0] = 0;
+  int m = 0;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] == 0) continue;
+    if (!src[i] || !dst[i]) return fail(WD_ERR_NULL_POINTER, "null range pointer");
+    unsigned char *s = nullptr, *d = nullptr;
+    int rc = device_view(src[i], dev, "src", &s);
+    if (rc != WD_OK) return rc;
+    rc = device_view(dst[i], dev, "dst", &d);
+    if (rc != WD_OK) return rc;
+    c.src[m] = s;
+    c.dst[m] = d;
+    c.bytes[m] = bytes[i];
+    c.vec[m] = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0;
+    c.first[m + 1] = c.first[m] + (bytes[i] + 15) / 16;
+    ++m;
+  }
+  c.n = m;
+  if (m == 0) return WD_OK;
+  DeviceInfo* di = nullptr;
+  const int rc = device_info(&di);
+  if (rc != WD_OK) return rc;
+  const unsigned long long units = c.first[m];
+  const unsigned long long per_cta = (unsigned long long)wdb::COPY_THREADS * wdb::COPY_UNROLL;
+  const unsigned grid = (unsigned)std::min<unsigned long long>((units + per_cta - 1) / per_cta,
+                                                               (unsigned long long)di->sm_count * 4);
+  wdb::copy_ranges_kernel<<<grid, wdb::COPY_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(c);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return fail(WD_ERR_CUDA, std::string("copy launch: ") + cudaGetErrorString(err));
   note_launch();
   return WD_OK;
 }
