@@ -10,7 +10,11 @@
 //
 // Design (B200):
 //  * Cooperative persistent grid, one CTA per SM (all CTAs co-resident),
-//    8 warps.  Every warp owns a ring of `depth` shared-memory slots and
+//    up to FFN_MAX_WARPS warps (the launch's block size; the host takes the
+//    most that fit next to a two-slot ring per warp: more warps spread the
+//    CTA's gate_up items and down chunks thinner, so the busiest warp's
+//    share of the weight stream, not the CTA's, sets the phase times).
+//    Every warp owns a ring of `depth` shared-memory slots and
 //    feeds it itself: after consuming stage s it issues stage s + depth with
 //    cp.async.bulk (no producer warp to wake, no empty barriers).  A warp's
 //    stage sequence is its gate_up stages (items (group, neuron): gate and up
@@ -67,18 +71,28 @@ struct FfnArgs {
   TpArgs tp;        // fused all-reduce (kTP): y = bf16 sum over the group's ranks
 };
 
-constexpr int FFN_THREADS = NWARPS * 32;
+// Warps of one CTA: at most FFN_MAX_WARPS (launch bounds), chosen per call.
+// Measured on B200 (H 4096, I 192, E 128, top-8, cold, us, 8 -> 11 warps):
+// B = 1 22.7 -> 20.5, B = 2 30.8 -> 26.6, B = 4 43.1 -> 40.0; 12 warps no
+// better at B = 1, 2 and too large for B = 4; 6 warps slower.
+constexpr int FFN_MAX_WARPS = 11;
+constexpr int FFN_THREADS = FFN_MAX_WARPS * 32;
+// ctrl words: [0] abort flag, [FFN_CTRL_ISSUED + w] stages issued by warp w,
+// [FFN_CTRL_POS + w] stages it consumed (read back after an abort).
+constexpr int FFN_CTRL_ISSUED = 4;
+constexpr int FFN_CTRL_POS = FFN_CTRL_ISSUED + FFN_MAX_WARPS;
+static_assert(FFN_CTRL_POS + FFN_MAX_WARPS <= CTRL_INTS, "ctrl words");
 constexpr int FFN_MAX_SLOTS = 64;  // B * topk of one single-launch call
 
 // Grid-barrier counter used when the caller passes none (one per device,
 // zero at module load).
 __device__ unsigned long long g_wd_ffn_sync = 0ull;
 
-__host__ inline int ffn_smem_bytes(int depth, int stage_bytes, int xh_bytes, int B, int rows_max,
-                                   int n, int E, bool dedup) {
-  return NWARPS * depth * stage_bytes + ((xh_bytes + 127) / 128) * 128 +
-         ((NWARPS * B * rows_max * 4 + 127) / 128) * 128 + ((n * 4 + 127) / 128) * 128 +
-         (NWARPS * depth + 1) * 8 + CTRL_INTS * 4 + route_smem_bytes(n, E, dedup);
+__host__ inline int ffn_smem_bytes(int nw, int depth, int stage_bytes, int xh_bytes, int B,
+                                   int rows_max, int n, int E, bool dedup) {
+  return nw * depth * stage_bytes + ((xh_bytes + 127) / 128) * 128 +
+         ((nw * B * rows_max * 4 + 127) / 128) * 128 + ((n * 4 + 127) / 128) * 128 +
+         (nw * depth + 1) * 8 + CTRL_INTS * 4 + route_smem_bytes(n, E, dedup);
 }
 
 // Generic-proxy reads of a shared-memory slot before an async-proxy (bulk
@@ -152,7 +166,7 @@ __device__ __forceinline__ void ffn_down_stage(const uint8_t* st, int row_bytes,
 
 template <bool kTP>
 __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a) {
-  constexpr int NCW = NWARPS;
+  const int NCW = (int)(blockDim.x >> 5);  // warps of this launch (<= FFN_MAX_WARPS)
   constexpr int WB = 2;  // bf16 weights
   extern __shared__ __align__(128) uint8_t smem[];
   const int depth = a.depth;
@@ -175,7 +189,8 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
   p += ((n * 4 + 127) / 128) * 128;
   uint64_t* full = reinterpret_cast<uint64_t*>(p);
   uint64_t* xbar = full + nslots;
-  // ctrl: [0] abort, [8+w] stages issued by warp w, [16+w] stages consumed.
+  // ctrl: [0] abort, [FFN_CTRL_ISSUED + w] stages issued by warp w,
+  // [FFN_CTRL_POS + w] stages consumed.
   volatile int* ctrl = reinterpret_cast<int*>(xbar + 1);
   int* route_base = const_cast<int*>(ctrl) + CTRL_INTS;
 
@@ -388,14 +403,15 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
     const uint4* src = reinterpret_cast<const uint4*>(a.h);
     uint4* dst = reinterpret_cast<uint4*>(hs);
     const int nv = (int)(h_bytes / 16);
-    for (int i = threadIdx.x; i < nv; i += 4 * FFN_THREADS) {
+    const int nt = (int)blockDim.x;
+    for (int i = threadIdx.x; i < nv; i += 4 * nt) {
       uint4 v[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        if (i + q * FFN_THREADS < nv) v[q] = ldcg16(src + i + q * FFN_THREADS);
+        if (i + q * nt < nv) v[q] = ldcg16(src + i + q * nt);
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        if (i + q * FFN_THREADS < nv) dst[i + q * FFN_THREADS] = v[q];
+        if (i + q * nt < nv) dst[i + q * nt] = v[q];
     }
   }
   __syncthreads();
@@ -417,8 +433,8 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
     }
   }
   if (lane == 0) {
-    ctrl[8 + warp] = issued;
-    ctrl[16 + warp] = pos;
+    ctrl[FFN_CTRL_ISSUED + warp] = issued;
+    ctrl[FFN_CTRL_POS + warp] = pos;
   }
   __syncthreads();
   if (ctrl[0]) {
@@ -427,7 +443,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 1) moe_ffn_kernel(const FfnArgs a
     // all-reduce the call still counts (epochs stay in step with the peers,
     // which time out on this rank's missing packets).
     if (lane == 0)
-      for (int q = ctrl[16 + warp]; q < ctrl[8 + warp]; ++q)
+      for (int q = ctrl[FFN_CTRL_POS + warp]; q < ctrl[FFN_CTRL_ISSUED + warp]; ++q)
         if (!mbar_wait(&my_full[q % depth], (uint32_t)(q / depth) & 1u)) break;
     if (kTP && threadIdx.x == 0)
       for (int c2 = (int)blockIdx.x; c2 < a.tp.max_ctas; c2 += G) a.tp.epochs[c2] = tp_ep;

@@ -988,33 +988,35 @@ int down_impl(const void* h, const uint8_t* w, const uint8_t* wscale, const int3
 
 // ---- single-launch FFN ------------------------------------------------------
 struct FfnPlan {
+  int nw = 0;  // warps per CTA (block size / 32)
   int depth = 0, kc = 0, rc = 0, rows_max = 0, stage_bytes = 0, xh_bytes = 0;
   int smem = 0, grid = 0;
   bool dedup = false;
 };
 
 // Whether moe_ffn_kernel runs on this device with `smem` bytes of shared
-// memory at one CTA per SM (cooperative launch: all CTAs co-resident).
-bool ffn_fits(const DeviceInfo* dev, int smem) {
+// memory and nw warps at one CTA per SM (cooperative launch: all CTAs
+// co-resident).
+bool ffn_fits(const DeviceInfo* dev, int smem, int nw) {
   static std::mutex mu;
-  static std::vector<std::array<int, 3>> cache;  // {device, smem, fits}
+  static std::vector<std::array<int, 4>> cache;  // {device, smem, nw, fits}
   int devno = 0;
   cudaGetDevice(&devno);
   {
     std::lock_guard<std::mutex> lock(mu);
     for (const auto& c : cache)
-      if (c[0] == devno && c[1] == smem) return c[2] != 0;
+      if (c[0] == devno && c[1] == smem && c[2] == nw) return c[3] != 0;
   }
   int nb = 0;
-  // both instantiations: one CTA per SM of 256 threads, the same shared memory
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, wdb::moe_ffn_kernel<true>,
-                                                    wdb::FFN_THREADS, (size_t)smem) != cudaSuccess) {
+  // both instantiations: the same registers and shared memory
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, wdb::moe_ffn_kernel<true>, nw * 32,
+                                                    (size_t)smem) != cudaSuccess) {
     cudaGetLastError();
     nb = 0;
   }
   (void)dev;
   std::lock_guard<std::mutex> lock(mu);
-  cache.push_back({devno, smem, nb >= 1 ? 1 : 0});
+  cache.push_back({devno, smem, nw, nb >= 1 ? 1 : 0});
   return nb >= 1;
 }
 
@@ -1066,15 +1068,20 @@ bool ffn_plan(const DeviceInfo* dev, int B, int E, int topk, int hidden, int int
   if (max_slots < wdb::FFN_MAX_SLOTS && n * nch > 64) return false;
   p.xh_bytes = std::max(B * hidden * 2, n * inter * 2);
   p.dedup = dedup;
+  // The most warps that fit (each with a ring of at least two slots), then
+  // the deepest ring for them (kernel comment in wd_ffn.cuh: measured).
   const int budget = dev->smem_optin - 2048;
-  for (int depth : {4, 3, 2}) {
-    const int need = wdb::ffn_smem_bytes(depth, p.stage_bytes, p.xh_bytes, B, p.rows_max, n, E,
-                                         dedup);
-    if (need <= budget && ffn_fits(dev, need)) {
-      p.depth = depth;
-      p.smem = need;
-      *pl = p;
-      return true;
+  for (int nw = wdb::FFN_MAX_WARPS; nw >= 4; --nw) {
+    for (int depth : {4, 3, 2}) {
+      const int need = wdb::ffn_smem_bytes(nw, depth, p.stage_bytes, p.xh_bytes, B, p.rows_max,
+                                           n, E, dedup);
+      if (need <= budget && ffn_fits(dev, need, nw)) {
+        p.nw = nw;
+        p.depth = depth;
+        p.smem = need;
+        *pl = p;
+        return true;
+      }
     }
   }
   return false;
@@ -1110,7 +1117,7 @@ int ffn_launch(const DeviceInfo* dev, const FfnPlan& p, const void* x, const voi
   attr[0].val.cooperative = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
-  cfg.blockDim = dim3(wdb::FFN_THREADS);
+  cfg.blockDim = dim3((unsigned)(p.nw * 32));
   cfg.dynamicSmemBytes = (size_t)p.smem;
   cfg.stream = s;
   cfg.attrs = attr;
