@@ -728,7 +728,7 @@ def exchange_record(fused, B, H, world):
     if world == 1 or fused is None or not fused.applies(B):
         return None
     one_shot = B * H * 8 * (world - 1)
-    two_shot = world >= 4 and one_shot > int(os.environ.get("WARP_DECODE_TP_TWO_SHOT_BYTES") or 512 << 10)
+    two_shot = world >= 4 and one_shot > int(os.environ.get("WARP_DECODE_TP_TWO_SHOT_BYTES") or 16 << 20)
     sent = 2 * B * H * 8 * (world - 1) // world if two_shot else one_shot
     return {"shape": "two-shot" if two_shot else "one-shot", "bytes_sent_per_rank": sent}
 

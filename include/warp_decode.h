@@ -312,8 +312,9 @@ WD_API int wd_tp_comm_destroy(void* comm);
 /*
  * Exchange shape of later calls on `comm` (no counterpart in the reference):
  * 0 = by size (default: one-shot with two ranks, and while a rank would
- * send at most 512 KiB, B x hidden x 8 x (world - 1) bytes;
- * WARP_DECODE_TP_TWO_SHOT_BYTES moves the threshold), 1 = one-shot (every rank sums every row), 2 = two-shot
+ * send at most 16 MiB, B x hidden x 8 x (world - 1) bytes;
+ * WARP_DECODE_TP_TWO_SHOT_BYTES moves the threshold), 1 = one-shot (every
+ * rank sums every row), 2 = two-shot
  * (row j summed by rank (j / 4) % world, which sends the bf16 result to the
  * others).  Both give the same bits.  Every rank must set the same mode.
  */

@@ -1375,12 +1375,17 @@ struct TpComm {
 
 // Bytes a rank sends one-shot (B x hidden x 8 x (world - 1)) above which the
 // automatic choice takes the two-shot exchange (from four ranks up), which
-// sends about 2 / world of that at the price of a second NVLink latency.
+// sends about 2 / world of that at the price of a second NVLink latency and
+// of the owners' wait for every rank.  Measured on four B200s (H 4096,
+// I 192 per rank, cold us; one-shot vs two-shot): B = 8 78.5 vs 86.3,
+// B = 16 100.9 vs 108.6, B = 32 132.8 vs 144.2, B = 64 (6 MiB sent
+// one-shot) 151.2 vs 168.3 -- the one-shot exchange costs about the same
+// from 0.25 to 6 MiB, so two-shot is kept for larger transfers only.
 // WARP_DECODE_TP_TWO_SHOT_BYTES overrides it.
 size_t tp_two_shot_bytes() {
   static const size_t v = [] {
     const char* e = std::getenv("WARP_DECODE_TP_TWO_SHOT_BYTES");
-    return e && *e ? (size_t)std::strtoull(e, nullptr, 10) : (size_t)(512u << 10);
+    return e && *e ? (size_t)std::strtoull(e, nullptr, 10) : (size_t)(16u << 20);
   }();
   return v;
 }

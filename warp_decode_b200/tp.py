@@ -99,7 +99,7 @@ class FusedAllReduce:
         """Whether a call of B tokens fits the communicator (B <= max_tokens).
 
         The exchange shape follows the size (one-shot with two ranks and up to
-        512 KiB sent per rank, two-shot above, which sends about 2/world of the
+        16 MiB sent per rank, two-shot above, which sends about 2/world of the
         one-shot bytes), so the fused path replaces NCCL at every batch the
         buffer holds.
         """
