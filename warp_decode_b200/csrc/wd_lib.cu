@@ -1379,8 +1379,9 @@ struct TpComm {
 // of the owners' wait for every rank.  Measured on four B200s (H 4096,
 // I 192 per rank, cold us; one-shot vs two-shot): B = 8 78.5 vs 86.3,
 // B = 16 100.9 vs 108.6, B = 32 132.8 vs 144.2, B = 64 (6 MiB sent
-// one-shot) 151.2 vs 168.3 -- the one-shot exchange costs about the same
-// from 0.25 to 6 MiB, so two-shot is kept for larger transfers only.
+// one-shot) 151.2 vs 168.3; on eight, B = 64 (14.7 MiB) 158.8 vs 170.4 --
+// the one-shot exchange costs about the same from 0.25 to 15 MiB, so
+// two-shot is kept for larger transfers only.
 // WARP_DECODE_TP_TWO_SHOT_BYTES overrides it.
 size_t tp_two_shot_bytes() {
   static const size_t v = [] {
