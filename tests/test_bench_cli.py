@@ -49,3 +49,36 @@ def test_multi_gpu_needs_torchrun():
     r = run_bench("--gpus", "2", "--steps", "1", "--warmup", "0")
     assert r.returncode == 2
     assert "torchrun" in r.stderr
+
+
+def test_reference_arm_gpu_bar_absent_without_gpu():
+    # the same-box bar of the reference's own CUDA kernels needs a GPU and the
+    # rebuilt library; without them the key is present and null
+    r = run_bench("--impl", "reference", "--batches", "1", "--steps", "1", "--warmup", "0")
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert "reference_gpu_kernels" in line and line["reference_gpu_kernels"] is None
+
+
+class _Fused:
+    def __init__(self, max_tokens):
+        self.max_tokens = max_tokens
+
+    def applies(self, B):
+        return 1 <= B <= self.max_tokens
+
+
+def test_exchange_record(monkeypatch):
+    monkeypatch.delenv("WARP_DECODE_TP_TWO_SHOT_BYTES", raising=False)
+    H = 4096
+    assert bench.exchange_record(None, 8, H, 2) is None
+    assert bench.exchange_record(_Fused(64), 8, H, 1) is None
+    assert bench.exchange_record(_Fused(64), 128, H, 8) is None  # above the communicator
+    # one-shot: every partial row to every peer, 8-byte packets
+    r = bench.exchange_record(_Fused(64), 64, H, 8)
+    assert r == {"shape": "one-shot", "bytes_sent_per_rank": 64 * H * 8 * 7}
+    # two-shot above the threshold (from four ranks): ~2/world of the bytes
+    monkeypatch.setenv("WARP_DECODE_TP_TWO_SHOT_BYTES", str(1 << 20))
+    r = bench.exchange_record(_Fused(64), 64, H, 8)
+    assert r == {"shape": "two-shot", "bytes_sent_per_rank": 2 * 64 * H * 8 * 7 // 8}
+    assert bench.exchange_record(_Fused(64), 64, H, 2)["shape"] == "one-shot"
