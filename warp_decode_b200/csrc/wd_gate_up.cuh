@@ -143,8 +143,6 @@ __global__ void __maxnreg__(FMT == W_E4M3 ? 96 : 112) moe_gate_up_kernel(const G
   using F = GuFmt<FMT>;
   constexpr int NCW = NWARPS;
 
-  // Let a directly following down kernel start its prologue now.
-  pdl_launch_dependents();
 
   extern __shared__ __align__(128) uint8_t smem[];
   const int depth = a.depth;
@@ -352,6 +350,12 @@ __global__ void __maxnreg__(FMT == W_E4M3 ? 96 : 112) moe_gate_up_kernel(const G
     if (lane == 0) ctrl[16 + warp] = s;
   }
   __syncthreads();
+  // This CTA's h rows are written: a directly following down kernel launched
+  // with programmatic dependence may start once every CTA got here (it waits
+  // for this grid to finish before reading h).  Triggered at entry instead,
+  // the down grid launched early, could not take an SM until gate_up CTAs
+  // left (shared memory) and started later, not sooner.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   // After an abort, let every issued but unconsumed copy land before exit.
   if (ctrl[0] && warp < NCW && lane == 0) {
     for (int q = ctrl[16 + warp]; q < ctrl[8 + warp]; ++q)

@@ -188,8 +188,6 @@ template <bool kMx, int kRoute, bool kFused = false>
 __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const CUtensorMap& tm_x,
                                                 const CUtensorMap* tm_s, const GateUpTcArgs a,
                                                 const FusedCtx* fx = nullptr) {
-  if constexpr (!kFused) pdl_launch_dependents();
-
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* base = kFused ? fx->base : smem_raw + pad;
@@ -585,6 +583,10 @@ __device__ __forceinline__ void gate_up_tc_body(const CUtensorMap& tm_w, const C
 
   tc_fence_before();
   __syncthreads();
+  // h of this CTA is stored: a following down kernel launched with
+  // programmatic dependence may start once every CTA got here (as in
+  // moe_gate_up_kernel; it waits for this grid before reading h).
+  if (!kFused && threadIdx.x == 0) pdl_launch_dependents();
   if (!kFused && warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);

@@ -133,10 +133,13 @@ int device_info(DeviceInfo** out) {
 }
 
 // Programmatic dependent launch of down behind gate_up: opt-in
-// (WARP_DECODE_PDL=1).  Measured on B200 with CUDA-graph replay, the early
-// start made the pair slower (B=2: 43.1 vs 35.0 us, B=4: 53.5 vs 47.1 us):
-// the down CTAs cannot share an SM with a gate_up CTA (shared memory), and
-// the early-launched grid delays its clusters.
+// (WARP_DECODE_PDL=1).  Measured on B200 with CUDA-graph replay: with gate_up
+// triggering at its entry the pair was slower (B=2: 43.1 vs 35.0 us, B=4:
+// 53.5 vs 47.1, B=8: 64.7 vs 61.9) -- the down CTAs cannot share an SM with a
+// gate_up CTA (shared memory), and the early-launched grid delays its
+// clusters; with the trigger after each gate_up CTA's last h store (now) it
+// is level or a little ahead (B=6: 53.2 vs 53.4 us, B=8: 61.4 vs 61.9), too
+// little to make it the default.
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("WARP_DECODE_PDL");
